@@ -1,0 +1,82 @@
+// Host-side launchers of the fp64-emu B200 kernels (one translation unit per
+// stage).  All launches go to the caller's stream; none allocates memory.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdint>
+
+#include "f64e_params.h"
+
+namespace f64e {
+
+// ---- sizing (f64e_sizing.cu) ----
+void launch_row_stats(const double* X, int64_t rows, int64_t cols, int bits, int16_t* sft, float* lg,
+                      cudaStream_t s);
+void col_slabs(int64_t NF, int64_t K, int64_t* kslab, int* nslab);
+void launch_col_stats(const double* X, int64_t batch, int64_t K, int64_t N, int bits, int16_t* sft, float* lg,
+                      double* pmax, double* pss, cudaStream_t s);
+void launch_maxlg(const float* lgA, int64_t m, const float* lgB, int64_t n, float* out, cudaStream_t s);
+
+// ---- extraction (f64e_extract.cu) ----
+// Planes are K-major int8: plane t of an operand with `rows` rows lives at
+// planes + t * rows * Kp, row r at + r * Kp, Kp = K rounded up to 16 (the pad
+// columns are written as zeros).  Plane order: residues 0..P-1, then the two
+// correction planes at P and P + 1, whose roles (hi or q) the caller picks.
+struct ExtractArgs {
+  const double* X;      // operand
+  int64_t rows;         // rows of the K-major planes (batch * M, or batch * N)
+  int64_t K, Kp;        // extracted K window and plane pitch
+  int64_t ld, koff;     // [rows, K] layout: element (r, k) at X[r * ld + koff + k]
+  int64_t batch, N;     // [K, N] layout only: members and columns per member
+  const int16_t* sft;   // per-row (or per-column) shifts before widening
+  const float* maxlg;   // operand maxima of lg (WsHead::maxlg)
+  int bits;             // requested operand width
+  int use_corr;
+  int hi_plane, q_plane;  // plane indices of the correction digits
+  int8_t* planes;
+};
+void launch_extract_rows(const ExtractArgs& a, const ModTables& T, cudaStream_t s);  // X is [rows, K]
+void launch_extract_cols(const ExtractArgs& a, const ModTables& T, cudaStream_t s);  // X is [batch, K, N]
+
+// ---- modular GEMM (f64e_gemm.cu) ----
+struct GemmArgs {
+  int M, N, batch, P;
+  int Kp;              // plane pitch (bytes); the K extent seen by TMA
+  int nkb;             // 128-wide K blocks per slot
+  int corr_mode;       // 0 none, 1 one fused int32 plane (Ahi.Bq + Aq.Bhi), 2 two int32 planes
+  int ldn;             // row pitch (elements) of the residue / correction outputs
+  int8_t* res;         // [P * batch][M][ldn]
+  int32_t* corr;       // [1 or 2][batch][M][ldn]
+  int* status;
+  uint64_t wait_limit_ns;
+};
+bool encode_plane_map(CUtensorMap* map, const void* base, int64_t zdim, int64_t rows, int64_t Kp, int box_rows);
+int gemm_block_rows_a();
+int gemm_block_rows_b();
+cudaError_t launch_residue_gemm(const CUtensorMap& tA, const CUtensorMap& tB, const GemmArgs& g, const ModTables& T,
+                                int num_sms, cudaStream_t s);
+
+// ---- reference-form modular GEMM for validation (f64e_gemm_check.cu) ----
+// Plain dp4a kernel with the same inputs and outputs as the tcgen05 kernel;
+// used only by the library's self-check entry point.
+void launch_residue_gemm_check(const int8_t* Apl, const int8_t* Bpl, int64_t MF, int64_t NF, const GemmArgs& g,
+                               const ModTables& T, cudaStream_t s);
+
+// ---- reconstruction (f64e_recon.cu) ----
+struct ReconArgs {
+  const int8_t* res;     // [P][batch * M][ldn]
+  const void* corr;      // see corr_mode
+  int corr_mode;         // 0 none, 1 int32 [MF][ldn], 2 two int32 planes, 3 int64 [MF][ldn]
+  int64_t MF, M, N, ldn;
+  const int16_t* sftA;   // [batch * M], before widening
+  const int16_t* sftB;   // [batch * N], before widening
+  const float* maxlg;
+  int bits, exact;
+  double* C;             // [batch * M][N]
+};
+void launch_reconstruct(const ReconArgs& a, const ModTables& T, cudaStream_t s);
+
+}  // namespace f64e

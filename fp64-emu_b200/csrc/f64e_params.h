@@ -1,0 +1,39 @@
+// Parameter blocks shared by the host orchestration and the fp64-emu kernels.
+// Everything a kernel needs about the modulus set travels by value in
+// ModTables (under 2 KB of kernel-parameter space), so no call ever uploads
+// tables or keeps per-device caches: every launch is capture-safe.
+#pragma once
+
+#include <cstdint>
+
+namespace f64e {
+
+constexpr int kMaxP = 20;   // largest modulus count (reference: fp64_emu.cu:27)
+constexpr int kGroups = 5;  // packed Garner factor words, four int8 factors each
+
+struct ModTables {
+  int P;                       // number of moduli
+  float log2M;                 // CRT range in bits, capped at 126 (float sum, as the reference)
+  uint32_t p[kMaxP];           // moduli
+  uint32_t mdiv[kMaxP];        // floor(2^32 / p): residue quotient estimate
+  uint32_t off[kMaxP];         // largest multiple of p not above 2^31 (signed-residue bias)
+  uint32_t mu2[kMaxP];         // 2 * floor(2^31 / p): limb-sum Barrett multiplier
+  uint32_t c36[kMaxP];         // 2^36 mod p
+  uint32_t c18[kMaxP];         // 2^18 mod p
+  uint8_t pow2mod[kMaxP][38];  // 2^b mod p for b = 16..53 (undoing the 2^b extraction bias)
+  int32_t mp[kMaxP][kGroups];  // balanced (M_u mod p_t), u < t, four per word
+  int32_t minv[kMaxP];         // (M_t mod p_t)^-1
+  int64_t m64[2];              // products of moduli 0..6 and 7..13
+};
+
+// Device-resident scalars at the head of every workspace.  maxlg holds the
+// operand maxima of the per-row / per-column log2 norms; in a partitioned
+// multi-GPU run they are MAX-all-reduced between the sizing and compute
+// phases, so every rank derives the same operand width.
+struct WsHead {
+  float maxlg[2];
+  int32_t status;  // first bounded wait that timed out (0 = none)
+  int32_t pad;
+};
+
+}  // namespace f64e

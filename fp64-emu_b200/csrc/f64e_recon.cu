@@ -1,0 +1,159 @@
+// Balanced-Garner reconstruction, quantization correction and rescale
+// (reference: fp64_emu.cu:854-952).
+//
+// For each output element the P balanced residues r_t give mixed-radix digits
+//   d_t = bal( (r_t - sum_{u<t} d_u * (M_u mod p_t)) * (M_t mod p_t)^-1 mod p_t )
+// (M_u = p_0 ... p_{u-1}); the factors are int8 and packed four per word, so
+// the inner products are dp4a, and only the words holding u < t are visited.
+// The digits are unique, hence so is V = sum d_t M_t in [-M/2, M/2), which is
+// recombined by grouped Horner (7 moduli per int64 group) and one 128-bit
+// combine, plus the correction (Ahi.Bq + Aq.Bhi) * 2^(b-15); exact mode
+// rounds the 128-bit value once to double, the fast mode combines in fp64 with
+// the reference's fused multiply-adds.  The result is scaled by
+// 2^-(sA_i + sB_j).
+#include "f64e_device.cuh"
+#include "f64e_kernels.h"
+
+namespace f64e {
+
+namespace {
+
+// Correctly rounded (RNE) conversion of a signed 128-bit integer.
+__device__ __forceinline__ double i128_to_double(__int128 v) {
+  const bool neg = v < 0;
+  const unsigned __int128 u = neg ? (unsigned __int128)0 - (unsigned __int128)v : (unsigned __int128)v;
+  const uint64_t hi = (uint64_t)(u >> 64), lo = (uint64_t)u;
+  double m;
+  if (hi == 0) {
+    m = __ull2double_rn(lo);
+  } else {
+    // Keep the top 64 significant bits; fold the dropped tail into a sticky
+    // bit far below the rounding position.
+    const int sh = 64 - __clzll((long long)hi);  // 1..64
+    const uint64_t top = (sh == 64) ? hi : ((hi << (64 - sh)) | (lo >> sh));
+    const uint64_t tail = (sh == 64) ? lo : (lo & ((1ULL << sh) - 1ULL));
+    m = ldexp(__ull2double_rn(top | (tail ? 1ULL : 0ULL)), sh);
+  }
+  return neg ? -m : m;
+}
+
+template <int CM>
+__device__ __forceinline__ void load_corr(const ReconArgs& a, int64_t off, int64_t plane, int64_t (&cr)[4]) {
+  if (CM == 0) {
+#pragma unroll
+    for (int e = 0; e < 4; e++) cr[e] = 0;
+  } else if (CM == 1) {
+    const int4 v = *reinterpret_cast<const int4*>(static_cast<const int32_t*>(a.corr) + off);
+    cr[0] = v.x; cr[1] = v.y; cr[2] = v.z; cr[3] = v.w;
+  } else if (CM == 2) {
+    const int32_t* c = static_cast<const int32_t*>(a.corr);
+    const int4 v = *reinterpret_cast<const int4*>(c + off);
+    const int4 w = *reinterpret_cast<const int4*>(c + plane + off);
+    cr[0] = (int64_t)v.x + w.x; cr[1] = (int64_t)v.y + w.y; cr[2] = (int64_t)v.z + w.z; cr[3] = (int64_t)v.w + w.w;
+  } else {
+    const int64_t* c = static_cast<const int64_t*>(a.corr) + off;
+    const longlong2 v0 = *reinterpret_cast<const longlong2*>(c);
+    const longlong2 v1 = *reinterpret_cast<const longlong2*>(c + 2);
+    cr[0] = v0.x; cr[1] = v0.y; cr[2] = v1.x; cr[3] = v1.y;
+  }
+}
+
+}  // namespace
+
+// Block (64, 4): x spans 64 four-column chunks of a row, y four rows.
+template <int CM>
+__global__ void __launch_bounds__(256) reconstruct_kernel(const ReconArgs a, const ModTables T) {
+  const Gain gn = pick_gain(a.maxlg[0], a.maxlg[1], T.log2M, a.bits);
+  const int cshift = gn.bits_eff - 15;
+  const int P = T.P;
+  const int ng = (P + 6) / 7;
+  const int64_t nq = (a.N + 3) >> 2;
+  const int64_t plane = a.MF * a.ldn;
+  const bool vec_out = ((a.N & 3) == 0) && ((reinterpret_cast<uintptr_t>(a.C) & 15) == 0);
+  for (int64_t i = (int64_t)blockIdx.y * 4 + threadIdx.y; i < a.MF; i += (int64_t)gridDim.y * 4) {
+    const int sa = (int)a.sftA[i] + gn.g;
+    const int16_t* __restrict__ sB = a.sftB + (i / a.M) * a.N;
+    for (int64_t jq = (int64_t)blockIdx.x * 64 + threadIdx.x; jq < nq; jq += (int64_t)gridDim.x * 64) {
+      const int64_t j0 = jq << 2;
+      const int64_t off = i * a.ldn + j0;
+      int32_t dp[4][kGroups];
+#pragma unroll
+      for (int e = 0; e < 4; e++)
+#pragma unroll
+        for (int g = 0; g < kGroups; g++) dp[e][g] = 0;
+#pragma unroll
+      for (int t = 0; t < kMaxP; t++) {
+        if (t >= P) break;
+        const uint32_t rw = *reinterpret_cast<const uint32_t*>(a.res + t * plane + off);
+        const uint32_t p = T.p[t], md = T.mdiv[t];
+        const int mi = T.minv[t];
+#pragma unroll
+        for (int e = 0; e < 4; e++) {
+          const int rt = (int)(int8_t)(uint8_t)(rw >> (8 * e));
+          int acc = 0;
+#pragma unroll
+          for (int g = 0; g < (t + 3) / 4; g++) acc = __dp4a(dp[e][g], T.mp[t][g], acc);
+          // |y| < 2^27; the bias p * 2^21 makes it non-negative and below 2^30.
+          const int y = (rt - acc) * mi;
+          const int d = balance(mod_small((uint32_t)(y + (int)(p << 21)), p, md), p);
+          dp[e][t >> 2] |= (int32_t)((uint32_t)(uint8_t)(int8_t)d << (8 * (t & 3)));
+        }
+      }
+      int64_t cr[4];
+      load_corr<CM>(a, off, plane, cr);
+      double outv[4];
+#pragma unroll
+      for (int e = 0; e < 4; e++) {
+        int64_t a0 = 0, a1 = 0, a2 = 0;
+#pragma unroll
+        for (int t = kMaxP - 1; t >= 0; t--) {
+          if (t >= P) continue;
+          const int64_t d = (int64_t)(int8_t)(uint8_t)((uint32_t)dp[e][t >> 2] >> (8 * (t & 3)));
+          if (t >= 14) a2 = a2 * (int64_t)T.p[t] + d;
+          else if (t >= 7) a1 = a1 * (int64_t)T.p[t] + d;
+          else a0 = a0 * (int64_t)T.p[t] + d;
+        }
+        const int64_t j = j0 + e;
+        const int sh = -sa - (j < a.N ? (int)sB[j] + gn.g : 0);
+        if (a.exact) {
+          __int128 v = (ng == 3) ? (__int128)a2 : ((ng == 2) ? (__int128)a1 : (__int128)a0);
+          if (ng == 3) v = v * (__int128)T.m64[1] + a1;
+          if (ng >= 2) v = v * (__int128)T.m64[0] + a0;
+          v += (__int128)cr[e] * ((__int128)1 << cshift);
+          outv[e] = ldexp(i128_to_double(v), sh);
+        } else {
+          double v = (double)((ng == 3) ? a2 : ((ng == 2) ? a1 : a0));
+          if (ng == 3) v = fma(v, (double)T.m64[1], (double)a1);
+          if (ng >= 2) v = fma(v, (double)T.m64[0], (double)a0);
+          v += ldexp((double)cr[e], cshift);
+          outv[e] = ldexp(v, sh);
+        }
+      }
+      double* crow = a.C + i * a.N;
+      if (vec_out && j0 + 4 <= a.N) {
+        *reinterpret_cast<double2*>(crow + j0) = make_double2(outv[0], outv[1]);
+        *reinterpret_cast<double2*>(crow + j0 + 2) = make_double2(outv[2], outv[3]);
+      } else {
+#pragma unroll
+        for (int e = 0; e < 4; e++)
+          if (j0 + e < a.N) crow[j0 + e] = outv[e];
+      }
+    }
+  }
+}
+
+void launch_reconstruct(const ReconArgs& a, const ModTables& T, cudaStream_t s) {
+  if (a.MF <= 0 || a.N <= 0) return;
+  const int64_t nq = (a.N + 3) >> 2;
+  const dim3 grid((unsigned)std::min<int64_t>((nq + 63) / 64, 1 << 20),
+                  (unsigned)std::min<int64_t>((a.MF + 3) / 4, 65535));
+  const dim3 block(64, 4);
+  switch (a.corr_mode) {
+    case 0: reconstruct_kernel<0><<<grid, block, 0, s>>>(a, T); break;
+    case 1: reconstruct_kernel<1><<<grid, block, 0, s>>>(a, T); break;
+    case 2: reconstruct_kernel<2><<<grid, block, 0, s>>>(a, T); break;
+    default: reconstruct_kernel<3><<<grid, block, 0, s>>>(a, T); break;
+  }
+}
+
+}  // namespace f64e

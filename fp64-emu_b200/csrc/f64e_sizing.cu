@@ -1,0 +1,189 @@
+// Operand sizing: per-row (and per-column, for operands consumed in their
+// [K, N] layout) power-of-two shifts and log2 2-norms, and the operand maxima
+// of those norms that feed the Cauchy-Schwarz width rule.
+//
+// The shifts depend only on max |x|; the norms feed one float comparison per
+// call (the width rule), so they are reduced in exactly the reference's order
+// to keep the chosen width identical on every input:
+//   rows:    fp64_emu.cu:111-146 (256 thread-strided partials, then a 128..1
+//            pairwise tree),
+//   columns: fp64_emu.cu:152-189 with the slab count of fp64_emu.cu:1159-1162.
+// `s += v * v` is a fused multiply-add, as nvcc contracts it in the reference.
+#include "f64e_kernels.h"
+#include "f64e_device.cuh"
+
+namespace f64e {
+
+__device__ __forceinline__ void finish_stats(double m, double s2, int bits, int16_t* sft, float* lg) {
+  const int e = (m > 0.0 && isfinite(m)) ? ilogb(m) : 0;
+  const int sh = (bits - 1) - e;
+  *lg = (s2 > 0.0 && isfinite(s2)) ? (float)(0.5 * log2(s2) + sh) : (m > 0.0 ? INFINITY : -INFINITY);
+  *sft = (int16_t)sh;
+}
+
+// One CTA of 256 threads per row.  Loads are issued four ahead; the
+// accumulation order per thread is the plain strided order.
+__global__ void __launch_bounds__(256) row_stats_kernel(const double* __restrict__ X, int64_t rows,
+                                                        int64_t cols, int bits, int16_t* __restrict__ sft,
+                                                        float* __restrict__ lg) {
+  for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
+    const double* __restrict__ x = X + r * cols;
+    double mx = 0.0, ss = 0.0;
+    int64_t c = threadIdx.x;
+    for (; c + 768 < cols; c += 1024) {
+      const double v0 = __ldg(x + c), v1 = __ldg(x + c + 256), v2 = __ldg(x + c + 512), v3 = __ldg(x + c + 768);
+      mx = fmax(mx, fabs(v0));
+      ss = fma(v0, v0, ss);
+      mx = fmax(mx, fabs(v1));
+      ss = fma(v1, v1, ss);
+      mx = fmax(mx, fabs(v2));
+      ss = fma(v2, v2, ss);
+      mx = fmax(mx, fabs(v3));
+      ss = fma(v3, v3, ss);
+    }
+    for (; c < cols; c += 256) {
+      const double v = __ldg(x + c);
+      mx = fmax(mx, fabs(v));
+      ss = fma(v, v, ss);
+    }
+    __shared__ double sm[256], sq[256];
+    const int t = threadIdx.x;
+    sm[t] = mx;
+    sq[t] = ss;
+    __syncthreads();
+#pragma unroll
+    for (int s = 128; s >= 32; s >>= 1) {
+      if (t < s) {
+        sm[t] = fmax(sm[t], sm[t + s]);
+        sq[t] += sq[t + s];
+      }
+      __syncthreads();
+    }
+    if (t < 32) {
+      double m = sm[t], q = sq[t];
+#pragma unroll
+      for (int s = 16; s > 0; s >>= 1) {
+        const double mo = __shfl_down_sync(0xFFFFFFFFu, m, s);
+        const double qo = __shfl_down_sync(0xFFFFFFFFu, q, s);
+        m = fmax(m, mo);
+        q += qo;
+      }
+      if (t == 0) finish_stats(m, q, bits, &sft[r], &lg[r]);
+    }
+    __syncthreads();
+  }
+}
+
+// Column partials over one K slab per blockIdx.y: thread j owns global column
+// j of a [batch, K, N] operand (member j / N), reads coalesced across columns.
+__global__ void __launch_bounds__(256) col_partial_kernel(const double* __restrict__ X, int64_t totalcols,
+                                                          int64_t K, int64_t N, int64_t kslab,
+                                                          double* __restrict__ pmax, double* __restrict__ pss) {
+  const int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (j >= totalcols) return;
+  const int64_t b = j / N, n = j - b * N;
+  const int64_t k0 = (int64_t)blockIdx.y * kslab;
+  const int64_t k1 = min(k0 + kslab, K);
+  const double* __restrict__ base = X + b * K * N + n;
+  double mx = 0.0, ss = 0.0;
+  int64_t k = k0;
+  for (; k + 3 < k1; k += 4) {
+    const double v0 = __ldg(base + k * N), v1 = __ldg(base + (k + 1) * N), v2 = __ldg(base + (k + 2) * N),
+                 v3 = __ldg(base + (k + 3) * N);
+    mx = fmax(mx, fabs(v0));
+    ss = fma(v0, v0, ss);
+    mx = fmax(mx, fabs(v1));
+    ss = fma(v1, v1, ss);
+    mx = fmax(mx, fabs(v2));
+    ss = fma(v2, v2, ss);
+    mx = fmax(mx, fabs(v3));
+    ss = fma(v3, v3, ss);
+  }
+  for (; k < k1; k++) {
+    const double v = __ldg(base + k * N);
+    mx = fmax(mx, fabs(v));
+    ss = fma(v, v, ss);
+  }
+  pmax[(int64_t)blockIdx.y * totalcols + j] = mx;
+  pss[(int64_t)blockIdx.y * totalcols + j] = ss;
+}
+
+__global__ void __launch_bounds__(256) col_finalize_kernel(const double* __restrict__ pmax,
+                                                           const double* __restrict__ pss, int64_t totalcols,
+                                                           int nslab, int bits, int16_t* __restrict__ sft,
+                                                           float* __restrict__ lg) {
+  const int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (j >= totalcols) return;
+  double mx = 0.0, ss = 0.0;
+  for (int s = 0; s < nslab; s++) {
+    mx = fmax(mx, pmax[(int64_t)s * totalcols + j]);
+    ss += pss[(int64_t)s * totalcols + j];
+  }
+  finish_stats(mx, ss, bits, &sft[j], &lg[j]);
+}
+
+// Operand maxima of lg (max is order independent).  One CTA.
+__global__ void __launch_bounds__(1024) maxlg_kernel(const float* __restrict__ lgA, int64_t m,
+                                                     const float* __restrict__ lgB, int64_t n,
+                                                     float* __restrict__ out) {
+  float a = -INFINITY, b = -INFINITY;
+  for (int64_t i = threadIdx.x; i < m; i += blockDim.x) a = fmaxf(a, lgA[i]);
+  for (int64_t j = threadIdx.x; j < n; j += blockDim.x) b = fmaxf(b, lgB[j]);
+#pragma unroll
+  for (int s = 16; s > 0; s >>= 1) {
+    a = fmaxf(a, __shfl_xor_sync(0xFFFFFFFFu, a, s));
+    b = fmaxf(b, __shfl_xor_sync(0xFFFFFFFFu, b, s));
+  }
+  __shared__ float sa[32], sb[32];
+  if ((threadIdx.x & 31) == 0) {
+    sa[threadIdx.x >> 5] = a;
+    sb[threadIdx.x >> 5] = b;
+  }
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    const int nw = blockDim.x >> 5;
+    a = threadIdx.x < nw ? sa[threadIdx.x] : -INFINITY;
+    b = threadIdx.x < nw ? sb[threadIdx.x] : -INFINITY;
+#pragma unroll
+    for (int s = 16; s > 0; s >>= 1) {
+      a = fmaxf(a, __shfl_xor_sync(0xFFFFFFFFu, a, s));
+      b = fmaxf(b, __shfl_xor_sync(0xFFFFFFFFu, b, s));
+    }
+    if (threadIdx.x == 0) {
+      out[0] = a;
+      out[1] = b;
+    }
+  }
+}
+
+void launch_row_stats(const double* X, int64_t rows, int64_t cols, int bits, int16_t* sft, float* lg,
+                      cudaStream_t s) {
+  if (rows <= 0) return;
+  const unsigned grid = (unsigned)std::min<int64_t>(rows, 1 << 30);
+  row_stats_kernel<<<grid, 256, 0, s>>>(X, rows, cols, bits, sft, lg);
+}
+
+void col_slabs(int64_t NF, int64_t K, int64_t* kslab, int* nslab) {
+  int64_t nsl0 = 131072 / std::max<int64_t>(NF, 1);
+  nsl0 = std::min<int64_t>(std::max<int64_t>(nsl0, 1), 128);
+  *kslab = (K + nsl0 - 1) / nsl0;
+  *nslab = *kslab > 0 ? (int)((K + *kslab - 1) / *kslab) : 0;
+}
+
+void launch_col_stats(const double* X, int64_t batch, int64_t K, int64_t N, int bits, int16_t* sft, float* lg,
+                      double* pmax, double* pss, cudaStream_t s) {
+  const int64_t NF = batch * N;
+  if (NF <= 0) return;
+  int64_t kslab;
+  int nslab;
+  col_slabs(NF, K, &kslab, &nslab);
+  const unsigned gx = (unsigned)((NF + 255) / 256);
+  if (nslab > 0) col_partial_kernel<<<dim3(gx, nslab), 256, 0, s>>>(X, NF, K, N, kslab, pmax, pss);
+  col_finalize_kernel<<<gx, 256, 0, s>>>(pmax, pss, NF, nslab, bits, sft, lg);
+}
+
+void launch_maxlg(const float* lgA, int64_t m, const float* lgB, int64_t n, float* out, cudaStream_t s) {
+  maxlg_kernel<<<1, 1024, 0, s>>>(lgA, m, lgB, n, out);
+}
+
+}  // namespace f64e

@@ -1,0 +1,549 @@
+"""Throughput benchmark of the emulated-FP64 product (one JSON line on rank 0).
+
+Default workload: mm_nt, M = N = K = 8192, float64
+N(0,1) operands, default plan (14 moduli + 2 correction GEMMs).  A "step" is
+one complete product.  With --gpus N > 1 (launched under torchrun) the
+product is split into a 2-D grid of C blocks (2 -> 2x1, 4 -> 2x2, 8 -> 4x2):
+each rank owns one block, the shared operand slices are distributed once
+before timing, and the only collective in a step is the MAX all-reduce of
+the two sizing maxima; total work is fixed, so scaling is "strong".
+
+  value   device time (CUDA events, max over ranks) per step with inputs
+          resident in HBM, as emulated FP64 TFLOP/s = 2MNK / t
+  e2e     the same through the public API (fp64_emu.mm_nt, or the
+          partitioned path) with each step's inputs copied from pinned host
+          memory and the product copied back inside the timed region
+  roofline  the modular tensor-core GEMM (the dominant kernel): INT8 ops
+          per launch / its average duration over the timed region
+
+--impl reference runs the reference's own CUDA kernels (the build in
+oracle/_ref, compiled from the reference sources; the reference has no CPU
+implementation of this path) through its own Python API on one GPU, with
+the same workload and protocol; under torchrun only rank 0 runs it.
+"""
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+for _p in (ROOT, os.path.join(ROOT, "fp64-emu_b200")):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+import torch  # noqa: E402
+import torch.distributed as dist  # noqa: E402
+
+METRIC = "emulated FP64 TFLOP/s (2MNK/t) at n=8192"
+UNIT = "TFLOP/s"
+PROFILE_SUMMARY = os.path.join(ROOT, "profiles", "residue_gemm_tc_mm_nt_8192.md")
+
+WORKLOADS = {
+    # name: (kind, batch, M, N, K, dist, nprimes, corr)
+    "C1": ("mm_nt", 1, 128, 128, 4096, "randn", None, None),
+    "C2": ("mm_nt", 1, 8192, 8192, 8192, "randn", None, None),
+    "C3": ("mm", 1, 4096, 4096, 4096, "int20", None, None),
+    "C3r": ("mm", 1, 4096, 4096, 4096, "int20", 13, False),
+    "C4": ("mm_nt", 1, 16384, 16384, 16384, "wide30", None, None),
+    "C5": ("bmm_nt", 64, 1024, 1024, 1024, "unif", None, None),
+    # profiling case: same kernels as C2 at a quarter of the device footprint
+    "P4096": ("mm_nt", 1, 4096, 4096, 4096, "randn", None, None),
+}
+
+
+def log(*a):
+    print(*a, file=sys.stderr, flush=True)
+
+
+# --------------------------------------------------------------- clocks --
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+    FIELDS = ("index,uuid,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device):
+        self.proc = None
+        self.path = None
+        try:
+            self.uuid = str(torch.cuda.get_device_properties(device).uuid)
+        except Exception:
+            self.uuid = None
+
+    def start(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "50",
+                 "-f", self.path], stdout=subprocess.DEVNULL, stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        time.sleep(0.1)
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        time.sleep(0.06)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        rows = []
+        with open(self.path) as f:
+            for line in f:
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) < 10:
+                    continue
+                if self.uuid and self.uuid.replace("GPU-", "") not in parts[1]:
+                    continue
+                rows.append(parts)
+        os.unlink(self.path)
+        if not rows:
+            return None
+        sm = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        mx = [float(r[3]) for r in rows if r[3].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[6 + i].lower().startswith("active")})
+        pw = [float(r[4]) for r in rows if r[4].replace(".", "").isdigit()]
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows), "power_w_max": max(pw) if pw else None}
+
+
+# ---------------------------------------------------------------- inputs --
+def make_inputs(dist_name, batch, M, N, K, nt, device, seed=0):
+    """Seeded synthetic operands on the device (BASELINE configs' value
+    distributions; no public dataset exists for this path)."""
+    g = torch.Generator(device=device).manual_seed(seed)
+    shpA = (batch, M, K) if batch > 1 else (M, K)
+    shpB = ((batch, K, N) if nt else (batch, N, K)) if batch > 1 else ((K, N) if nt else (N, K))
+    opts = dict(dtype=torch.float64, device=device, generator=g)
+    if dist_name == "randn":
+        A, B = torch.randn(shpA, **opts), torch.randn(shpB, **opts)
+    elif dist_name == "unif":
+        A, B = torch.rand(shpA, **opts) * 2 - 1, torch.rand(shpB, **opts) * 2 - 1
+    elif dist_name == "int20":
+        lim = 1 << 20
+        A = torch.randint(-lim, lim + 1, shpA, device=device, generator=g).double()
+        B = torch.randint(-lim, lim + 1, shpB, device=device, generator=g).double()
+    elif dist_name == "wide30":
+        A, B = torch.randn(shpA, **opts), torch.randn(shpB, **opts)
+        A *= torch.exp2(torch.randint(-30, 31, shpA, device=device, generator=g).double())
+        B *= torch.exp2(torch.randint(-30, 31, shpB, device=device, generator=g).double())
+    else:
+        raise ValueError(dist_name)
+    return A, B
+
+
+def int8_peak_from_file():
+    """INT8 dense peak: B200's INT8 dense rate is twice its BF16 dense rate;
+    the BF16 figures are the pool's measured cuBLAS numbers."""
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            mp = json.load(f)
+        return 2.0 * float(mp["bf16_tflops_sustained"]), 2.0 * float(mp["bf16_tflops"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return 2.0 * 1400.0, 2.0 * 1590.0, "fallback"
+
+
+def profiled_traffic_per_launch():
+    """dram bytes (read + write) per GEMM launch from the committed ncu summary."""
+    try:
+        with open(PROFILE_SUMMARY) as f:
+            for line in f:
+                if line.strip().startswith("dram_bytes_per_launch"):
+                    return int(float(line.split("=")[1].split()[0]))
+    except (OSError, ValueError, IndexError):
+        pass
+    return None
+
+
+# ----------------------------------------------------------- our product --
+class Step:
+    """One rank's product, phase by phase on the current stream, with a
+    preallocated workspace (the public entry points allocate the same
+    workspace from torch's caching allocator per call)."""
+
+    def __init__(self, kind, A, B, nprimes, corr, slab_cols):
+        import fp64_emu
+        from fp64_emu.dist import ShardedProduct
+        self.nt = kind in ("mm_nt", "bmm_nt")
+        K = A.size(-1)
+        self.sp = ShardedProduct(A, B, self.nt, slab_cols, K, nprimes=nprimes, corr=corr)
+        shape = (A.size(0), A.size(1), B.size(-1) if self.nt else B.size(1)) if A.dim() == 3 else \
+            (A.size(0), B.size(-1) if self.nt else B.size(0))
+        self.out = torch.empty(shape, dtype=torch.float64, device=A.device)
+        self.nprimes, self.corr = self.sp.primes.numel(), self.sp.corr
+        self.fp64_emu = fp64_emu
+
+    def run(self, ev_g0=None, ev_g1=None):
+        sp, out = self.sp, self.out
+        sp.sizing(out)
+        sp._phase(out, 2)
+        if ev_g0 is not None:
+            ev_g0.record()
+        sp._phase(out, 4)
+        if ev_g1 is not None:
+            ev_g1.record()
+        sp._phase(out, 8)
+
+
+def barrier():
+    if dist.is_initialized():
+        dist.barrier()
+
+
+def max_over_ranks(x):
+    if not dist.is_initialized():
+        return x
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def our_kernel_launches_per_step(kind, batch, K):
+    # sizing: row stats of A + (column partial + finalize, or row stats) of B
+    # + operand maxima; extraction of A and B; one GEMM; one reconstruction.
+    nt = kind in ("mm_nt", "bmm_nt")
+    return (1 + (2 if nt else 1) + 1) + 2 + 1 + 1
+
+
+def cpu_baseline_oracle(A_cpu, Bt_cpu, nprimes, corr, rows):
+    """The CPU restatement oracle on a bounded sample: `rows` rows of A against
+    the whole of Bt (all of B's extraction, a slice of the GEMM)."""
+    from oracle import oracle as O
+    O.build()
+    threads = O.cpu_count()
+    O.set_threads(threads)
+    a = A_cpu[:rows].numpy()
+    b = Bt_cpu.numpy()
+    t0 = time.perf_counter()
+    O.emu(a, b, nprimes=nprimes, corr=corr, b_nt=True)
+    dt = time.perf_counter() - t0
+    M, K = a.shape
+    N = b.shape[1]
+    return {"value": 2.0 * M * N * K / dt / 1e12, "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": f"oracle/f64e_oracle.c, {M} rows of A x full Bt ({K}x{N}), one product, {dt:.1f} s"}
+
+
+def cpu_fp64_torch(A_cpu, Bt_cpu, rows):
+    threads = os.cpu_count()
+    torch.set_num_threads(threads)
+    a = A_cpu[:rows]
+    a @ Bt_cpu[:, :64]
+    t0 = time.perf_counter()
+    a @ Bt_cpu
+    dt = time.perf_counter() - t0
+    return {"value": 2.0 * a.size(0) * Bt_cpu.size(1) * a.size(1) / dt / 1e12, "unit": UNIT, "cores": threads,
+            "sample": f"torch.mm float64 on host, {a.size(0)}x{a.size(1)} @ {Bt_cpu.size(0)}x{Bt_cpu.size(1)}"}
+
+
+def run_ours(args):
+    kind, batch, M, N, K, dist_name, nprimes, corr = WORKLOADS[args.workload]
+    rank, world = (dist.get_rank(), dist.get_world_size()) if dist.is_initialized() else (0, 1)
+    dev = torch.device("cuda", torch.cuda.current_device())
+    nt = kind in ("mm_nt", "bmm_nt")
+    from fp64_emu import plan_config
+    from fp64_emu.dist import block_range, grid_shape, rank_block
+    if nprimes is None or corr is None:
+        dp, dc = plan_config(K)
+        nprimes = dp if nprimes is None else nprimes
+        corr = dc if corr is None else corr
+
+    # Full operands are generated from one seed on rank 0 (the shared operand's
+    # slices reach the other ranks by one NCCL broadcast, outside timing).
+    A, B = make_inputs(dist_name, batch, M, N, K, nt, dev, seed=args.seed) if rank == 0 else (None, None)
+    if world > 1:
+        if batch > 1:
+            shp_a, shp_b = (batch, M, K), ((batch, K, N) if nt else (batch, N, K))
+        else:
+            shp_a, shp_b = (M, K), ((K, N) if nt else (N, K))
+        if rank != 0:
+            A = torch.empty(shp_a, dtype=torch.float64, device=dev)
+            B = torch.empty(shp_b, dtype=torch.float64, device=dev)
+        t0 = time.perf_counter()
+        dist.broadcast(A, 0)
+        dist.broadcast(B, 0)
+        torch.cuda.synchronize()
+        bcast_s = time.perf_counter() - t0
+    else:
+        bcast_s = 0.0
+    if batch > 1:
+        b0, b1 = block_range(batch, world, rank)
+        A_l, B_l = A[b0:b1].contiguous(), B[b0:b1].contiguous()
+        slab_cols = batch * N
+        work = 2.0 * batch * M * N * K
+        part = f"batch split {world}"
+    else:
+        (r0, r1), (c0, c1) = rank_block(rank, world, M, N)
+        A_l = A[r0:r1].contiguous()
+        B_l = (B[:, c0:c1] if nt else B[c0:c1]).contiguous()
+        slab_cols = N
+        work = 2.0 * M * N * K
+        pr, pc = grid_shape(world)
+        part = f"2-D C blocks {pr}x{pc}"
+    A_host_full = A.cpu() if (rank == 0 and world == 1 and not args.no_cpu) else None
+    B_host_full = B.cpu() if (rank == 0 and world == 1 and not args.no_cpu) else None
+    del A, B
+    torch.cuda.empty_cache()
+
+    step = Step(kind, A_l, B_l, nprimes, corr, slab_cols)
+    for _ in range(args.warmup):
+        step.run()
+    torch.cuda.synchronize()
+
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    clocks = ClockSampler(dev)
+    clocks.start()
+    barrier()
+    torch.cuda.synchronize()
+    t_start = torch.cuda.Event(enable_timing=True)
+    t_stop = torch.cuda.Event(enable_timing=True)
+    t_start.record()
+    for i in range(args.steps):
+        step.run(ev[i][0], ev[i][1])
+    t_stop.record()
+    torch.cuda.synchronize()
+    barrier()
+    ms_local = t_start.elapsed_time(t_stop) / args.steps
+    gemm_ms_local = sum(a.elapsed_time(b) for a, b in ev) / args.steps
+
+    # e2e through the public API with host buffers.
+    import fp64_emu
+    A_pin = A_l.cpu().pin_memory()
+    B_pin = B_l.cpu().pin_memory()
+    out_pin = torch.empty(step.out.shape, dtype=torch.float64).pin_memory()
+    A_d = torch.empty_like(A_l)
+    B_d = torch.empty_like(B_l)
+
+    def e2e_step():
+        A_d.copy_(A_pin, non_blocking=True)
+        B_d.copy_(B_pin, non_blocking=True)
+        if world == 1:
+            C = {"mm_nt": fp64_emu.mm_nt, "mm": fp64_emu.mm, "bmm_nt": fp64_emu.bmm_nt,
+                 "bmm": fp64_emu.bmm}[kind](A_d, B_d, nprimes=nprimes, corr=corr)
+        else:
+            from fp64_emu.dist import ShardedProduct
+            C = torch.empty(step.out.shape, dtype=torch.float64, device=dev)
+            ShardedProduct(A_d, B_d, nt, slab_cols, K, nprimes=nprimes, corr=corr).run(C)
+        out_pin.copy_(C, non_blocking=True)
+
+    e2e_steps = max(3, min(args.steps, 20))
+    for _ in range(2):
+        e2e_step()
+    torch.cuda.synchronize()
+    barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(e2e_steps):
+        e2e_step()
+    e1.record()
+    torch.cuda.synchronize()
+    barrier()
+    e2e_ms_local = e0.elapsed_time(e1) / e2e_steps
+    clk = clocks.stop()
+
+    ms = max_over_ranks(ms_local)
+    gemm_ms = max_over_ranks(gemm_ms_local)
+    e2e_ms = max_over_ranks(e2e_ms_local)
+    h2d = (A_l.numel() + B_l.numel()) * 8
+    d2h = step.out.numel() * 8
+
+    # Roofline of the dominant kernel on this rank.
+    G = nprimes + (2 if corr else 0)
+    Ml, Kl = A_l.shape[-2], A_l.shape[-1]
+    Nl = B_l.shape[-1] if nt else B_l.shape[-2]
+    bl = A_l.shape[0] if A_l.dim() == 3 else 1
+    int8_ops = 2.0 * G * bl * Ml * Nl * Kl
+    achieved = int8_ops / (gemm_ms_local * 1e-3) / 1e12
+    peak_sus, peak_burst, src = int8_peak_from_file()
+    traffic = profiled_traffic_per_launch() if (args.workload == "C2" and world == 1) else None
+
+    result = {
+        "metric": METRIC if args.workload == "C2" else f"emulated FP64 TFLOP/s (2MNK/t), {args.workload}",
+        "value": round(work / (ms * 1e-3) / 1e12, 3),
+        "unit": UNIT,
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms, 4),
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "f64",
+        "data": "synthetic",
+        "config": {"workload": f"{args.workload}: {kind} batch={batch} M={M} N={N} K={K} {dist_name}, "
+                               f"plan nprimes={nprimes} corr={corr} ({G} INT8 GEMMs per product)",
+                   "parallelism": part, "l2": "operands larger than L2 (no flush)",
+                   "compute": "s8 x s8 -> s32 tcgen05 residue GEMMs, exact int128 recombine"},
+        "e2e": {"value": round(work / (e2e_ms * 1e-3) / 1e12, 3), "unit": UNIT, "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h, "api": "fp64_emu." + kind if world == 1 else "fp64_emu.dist"},
+        "gpu_launches": our_kernel_launches_per_step(kind, batch, K) * args.steps,
+        "roofline": {"bound": "tensor", "kernel": "residue_gemm_tc_kernel", "achieved": round(achieved, 1),
+                     "peak": round(peak_sus, 1), "unit": "TOPS (int8)", "frac": round(achieved / peak_sus, 4),
+                     "peak_note": f"INT8 dense = 2 x bf16 dense ({src} MEASURED_PEAKS.json, sustained; "
+                                  f"burst {peak_burst:.0f})",
+                     "gemm_ms_per_step": round(gemm_ms, 4), "traffic": traffic},
+        "phases_ms": {"gemm": round(gemm_ms, 4), "other": round(ms - gemm_ms, 4)},
+        "clocks": clk,
+    }
+    if world > 1:
+        result["operand_broadcast_s"] = round(bcast_s, 3)
+    if rank == 0 and world == 1 and not args.no_cpu and batch == 1 and nt:
+        try:
+            result["cpu_baseline"] = cpu_baseline_oracle(A_host_full, B_host_full, nprimes, corr,
+                                                         rows=args.cpu_rows)
+        except Exception as e:  # noqa: BLE001
+            result["cpu_baseline"] = {"value": None, "error": str(e)[:200]}
+        try:
+            result["cpu_fp64_torch"] = cpu_fp64_torch(A_host_full, B_host_full, rows=1024)
+        except Exception as e:  # noqa: BLE001
+            result["cpu_fp64_torch"] = {"value": None, "error": str(e)[:200]}
+    if rank == 0 and not args.no_native:
+        result["native_dgemm"] = native_dgemm(A_l, B_l, nt, args)
+    if rank == 0:
+        print(json.dumps(result), flush=True)
+
+
+def native_dgemm(A, B, nt, args):
+    """cuBLAS DGEMM on the same per-rank operands, for context."""
+    f = (lambda: torch.matmul(A, B)) if nt else (lambda: torch.matmul(A, B.transpose(-1, -2)))
+    for _ in range(2):
+        f()
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    n = max(3, min(args.steps, 10))
+    s.record()
+    for _ in range(n):
+        f()
+    e.record()
+    torch.cuda.synchronize()
+    ms = s.elapsed_time(e) / n
+    Ml, Kl = A.shape[-2], A.shape[-1]
+    Nl = B.shape[-1] if nt else B.shape[-2]
+    bl = A.shape[0] if A.dim() == 3 else 1
+    return {"value": round(2.0 * bl * Ml * Nl * Kl / (ms * 1e-3) / 1e12, 3), "unit": UNIT, "ms": round(ms, 4)}
+
+
+# ------------------------------------------------------------ reference --
+def load_reference():
+    ref_dir = os.path.join(ROOT, "oracle", "_ref")
+    if not os.path.exists(os.path.join(ref_dir, "fp64_emu_ref.so")):
+        return None, "reference build oracle/_ref/fp64_emu_ref.so missing (python oracle/build_ref.py)"
+    if ref_dir not in sys.path:
+        sys.path.insert(0, ref_dir)
+    import fp64_emu_ref
+    return fp64_emu_ref, None
+
+
+def run_reference(args):
+    rank = dist.get_rank() if dist.is_initialized() else 0
+    if rank != 0:
+        return
+    R, why = load_reference()
+    kind, batch, M, N, K, dist_name, nprimes, corr = WORKLOADS[args.workload]
+    if R is None:
+        print(json.dumps({"impl": "reference", "unavailable": why}), flush=True)
+        return
+    dev = torch.device("cuda", torch.cuda.current_device())
+    nt = kind in ("mm_nt", "bmm_nt")
+    A, B = make_inputs(dist_name, batch, M, N, K, nt, dev, seed=args.seed)
+    fn = getattr(R, kind)
+    kw = {}
+    if nprimes is not None:
+        kw["nprimes"] = nprimes
+    if corr is not None:
+        kw["corr"] = corr
+    for _ in range(args.warmup + 1):   # the first call runs the reference's dispatch probe
+        fn(A, B, **kw)
+    torch.cuda.synchronize()
+    clocks = ClockSampler(dev)
+    clocks.start()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(args.steps):
+        fn(A, B, **kw)
+    e.record()
+    torch.cuda.synchronize()
+    ms = s.elapsed_time(e) / args.steps
+    A_pin, B_pin = A.cpu().pin_memory(), B.cpu().pin_memory()
+    C0 = fn(A, B, **kw)
+    out_pin = torch.empty(C0.shape, dtype=torch.float64).pin_memory()
+    A_d, B_d = torch.empty_like(A), torch.empty_like(B)
+
+    def e2e_step():
+        A_d.copy_(A_pin, non_blocking=True)
+        B_d.copy_(B_pin, non_blocking=True)
+        out_pin.copy_(fn(A_d, B_d, **kw), non_blocking=True)
+
+    n2 = max(3, min(args.steps, 20))
+    e2e_step()
+    torch.cuda.synchronize()
+    s.record()
+    for _ in range(n2):
+        e2e_step()
+    e.record()
+    torch.cuda.synchronize()
+    e2e_ms = s.elapsed_time(e) / n2
+    clk = clocks.stop()
+    work = 2.0 * batch * M * N * K
+    value = round(work / (ms * 1e-3) / 1e12, 3)
+    result = {
+        "impl": "reference",
+        "metric": METRIC if args.workload == "C2" else f"emulated FP64 TFLOP/s (2MNK/t), {args.workload}",
+        "value": value, "unit": UNIT, "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "f64", "data": "synthetic",
+        "config": {"workload": f"{args.workload}: {kind} batch={batch} M={M} N={N} K={K} {dist_name}, "
+                               f"reference default dispatch (first-call probe excluded)",
+                   "l2": "operands larger than L2 (no flush)"},
+        "e2e": {"value": round(work / (e2e_ms * 1e-3) / 1e12, 3), "unit": UNIT,
+                "h2d_bytes_per_step": (A.numel() + B.numel()) * 8, "d2h_bytes_per_step": C0.numel() * 8},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": 0, "kind": "reference",
+                         "sample": "the reference's own CUDA kernels (oracle/_ref, built from its sources) on "
+                                   "one B200: the reference has no CPU implementation of this path"},
+        "clocks": clk,
+    }
+    print(json.dumps(result), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=30)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--workload", default="C2", choices=sorted(WORKLOADS))
+    ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--cpu-rows", type=int, default=128)
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baselines")
+    ap.add_argument("--no-native", action="store_true", help="skip the cuBLAS DGEMM context number")
+    args = ap.parse_args()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    try:
+        if args.impl == "reference":
+            run_reference(args)
+        else:
+            run_ours(args)
+    finally:
+        if dist.is_initialized():
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -120,6 +120,38 @@ int get_tables(const int32_t* primes, int P, ModTables* out) {
       run = run * (primes[u] % pt) % pt;
     }
   }
+  // Fast-form constants (see ModTables).
+  T.fast_recon = 1;
+  for (int t = 0; t < P; t++) {
+    const uint64_t p = (uint64_t)primes[t];
+    uint32_t kl = 0, kh = 0;
+    for (int i = 0; i < 4; i++) kl |= (uint32_t)(((1ULL << (8 * i)) % p) & 0xFF) << (8 * i);
+    for (int i = 0; i < 3; i++) kh |= (uint32_t)(((1ULL << (8 * (i + 4))) % p) & 0xFF) << (8 * i);
+    T.kl[t] = kl;
+    T.kh[t] = kh;
+    T.mex[t] = (uint32_t)(((1ULL << 32) + p - 1) / p);
+    T.hh[t] = (uint32_t)(p / 2);
+    if (p <= 128) T.fast_recon = 0;
+    T.mrec[t] = (p > 128) ? (uint32_t)(((1ULL << 39) + p - 1) / p) : 0;
+  }
+  for (int t = 0; t < P; t++) {
+    const int64_t pt = primes[t];
+    int64_t run = 1 % pt;
+    int64_t csum = 0;  // sum_u h_u * (M_u mod p_t)
+    for (int u = 0; u < t; u++) {
+      T.cu[t][u >> 2] |= (uint32_t)(run & 0xFF) << (8 * (u & 3));
+      csum += (int64_t)(primes[u] / 2) * run;
+      run = run * (primes[u] % pt) % pt;
+    }
+    const int64_t kc = ((csum % pt) * T.minv[t] + pt / 2) % pt;
+    const int64_t B = pt * (((1LL << 29) + pt - 1) / pt);
+    T.krec[t] = (uint32_t)(kc + B);
+  }
+  for (int g = 0; g < 3; g++) {
+    int64_t hv = 0;
+    for (int t = std::min(g * 7 + 6, P - 1); t >= g * 7; t--) hv = hv * primes[t] + primes[t] / 2;
+    T.hoff[g] = hv;
+  }
   cache.emplace(key, T);
   *out = T;
   return F64E_OK;
@@ -178,7 +210,7 @@ int make_plan(const f64e_problem* p, Plan* L) {
   else l.recon_corr = l.deep ? 3 : l.gemm_corr;
   l.kslab = 0;
   l.nslab = 0;
-  if (nt) col_slabs(l.NF, l.K, &l.kslab, &l.nslab);
+  if (nt) col_slabs(p->slab_cols > 0 ? p->slab_cols : l.NF, l.K, &l.kslab, &l.nslab);
   size_t o = 256;  // WsHead
   auto take = [&](size_t bytes) {
     const size_t at = o;
@@ -241,8 +273,8 @@ int run_sizing(const Plan& l, const double* A, const double* B, void* ws, cudaSt
   if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync");
   launch_row_stats(A, l.MF, l.K, l.bits, at<int16_t>(ws, l.o_sftA), at<float>(ws, l.o_lgA), s);
   if (l.nt)
-    launch_col_stats(B, l.batch, l.K, l.N, l.bits, at<int16_t>(ws, l.o_sftB), at<float>(ws, l.o_lgB),
-                     at<double>(ws, l.o_pmax), at<double>(ws, l.o_pss), s);
+    launch_col_stats(B, l.batch, l.K, l.N, l.kslab, l.nslab, l.bits, at<int16_t>(ws, l.o_sftB),
+                     at<float>(ws, l.o_lgB), at<double>(ws, l.o_pmax), at<double>(ws, l.o_pss), s);
   else
     launch_row_stats(B, l.NF, l.K, l.bits, at<int16_t>(ws, l.o_sftB), at<float>(ws, l.o_lgB), s);
   launch_maxlg(at<float>(ws, l.o_lgA), l.MF, at<float>(ws, l.o_lgB), l.NF, head->maxlg, s);
@@ -367,11 +399,15 @@ int run(const f64e_problem* p, const double* A, const double* B, double* out, vo
   }
   if (!(phases & F64E_PHASE_COMPUTE)) return F64E_OK;
   if (!l.deep) {
-    run_extract(l, T, A, B, ws, 0, l.K, s);
+    if (phases & F64E_PHASE_EXTRACT) run_extract(l, T, A, B, ws, 0, l.K, s);
     if (ev) cudaEventRecord(ev[1], s);
-    rc = run_gemm(l, T, ws, d, checked, s);
-    if (rc) return rc;
-  } else {
+    if (phases & F64E_PHASE_GEMM) {
+      rc = run_gemm(l, T, ws, d, checked, s);
+      if (rc) return rc;
+    }
+  } else if (phases & (F64E_PHASE_EXTRACT | F64E_PHASE_GEMM)) {
+    if ((phases & (F64E_PHASE_EXTRACT | F64E_PHASE_GEMM)) != (F64E_PHASE_EXTRACT | F64E_PHASE_GEMM))
+      return fail(F64E_ERR_ARGUMENT, "deep-K products run EXTRACT and GEMM together");
     const int64_t nres = (int64_t)l.P * l.MF * l.ldn, ncorr = l.use_corr ? l.MF * l.ldn : 0;
     for (int sgi = 0; sgi < l.nseg; sgi++) {
       const int64_t k0 = (int64_t)sgi * l.Kseg;
@@ -388,7 +424,7 @@ int run(const f64e_problem* p, const double* A, const double* B, double* out, vo
     cudaEventRecord(ev[2], s);
     cudaEventRecord(ev[3], s);
   }
-  run_reconstruct(l, T, ws, out, s);
+  if (phases & F64E_PHASE_RECON) run_reconstruct(l, T, ws, out, s);
   if (ev) cudaEventRecord(ev[4], s);
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "kernel launch");
@@ -408,6 +444,7 @@ f64e_problem make_problem(int64_t batch, int64_t M, int64_t N, int64_t K, int32_
   p.exact = exact;
   p.bits = (bits < INT32_MIN || bits > INT32_MAX) ? 0 : (int32_t)bits;
   p.use_corr = use_corr;
+  p.slab_cols = 0;
   return p;
 }
 

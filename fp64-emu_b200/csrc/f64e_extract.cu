@@ -32,13 +32,14 @@ __device__ __forceinline__ uint64_t rne_shr(uint64_t mag, int s) {
 
 __device__ __forceinline__ int clamp127(int64_t v) { return v > 127 ? 127 : (v < -127 ? -127 : (int)v); }
 
-// Limbs of the biased scaled integer and the two correction digits of x.
-struct Limbs {
-  uint32_t a, b, c;
+// Biased scaled integer u = T*sign + 2^b (two's complement, mod 2^64) and
+// the two correction digits of one element.
+struct Split {
+  uint64_t u;
   int h, q;
 };
 
-__device__ __forceinline__ Limbs split_elem(double x, int s, int be, bool corr) {
+__device__ __forceinline__ Split split_elem(double x, int s, int be, bool corr) {
   const uint64_t xb = (uint64_t)__double_as_longlong(x);
   const bool neg = (int64_t)xb < 0;
   const int e = (int)((xb >> 52) & 0x7FF);
@@ -47,27 +48,27 @@ __device__ __forceinline__ Limbs split_elem(double x, int s, int be, bool corr) 
   const int t = (e ? e : 1) - 1075 + s + 52;
   const uint64_t Tu = rne_shr(mag, 52 - t);
   const uint64_t td = neg ? (0ULL - Tu) : Tu;  // two's complement of the signed value
-  Limbs L;
+  Split S;
   if (corr) {
     const uint64_t r8 = rne_shr(mag, 44 - t) - (Tu << 8);
     const uint64_t h8 = rne_shr(Tu, be - 7);
-    L.h = clamp127((int64_t)(neg ? (0ULL - h8) : h8));
-    L.q = clamp127((int64_t)(neg ? (0ULL - r8) : r8));
+    S.h = clamp127((int64_t)(neg ? (0ULL - h8) : h8));
+    S.q = clamp127((int64_t)(neg ? (0ULL - r8) : r8));
   } else {
-    L.h = L.q = 0;
+    S.h = S.q = 0;
   }
-  const uint64_t uu = td + (1ULL << be);
-  L.a = (uint32_t)(uu >> 36);
-  L.b = (uint32_t)((uu >> 18) & 0x3FFFFu);
-  L.c = (uint32_t)(uu & 0x3FFFFu);
-  return L;
+  S.u = td + (1ULL << be);
+  return S;
 }
 
-// Balanced residue byte of one element for modulus index t; cb undoes the
-// 2^b bias (cb = p - (2^b mod p)).
-__device__ __forceinline__ uint32_t residue_byte(const Limbs& L, uint32_t p, uint32_t c36, uint32_t c18,
-                                                 uint32_t cb, uint32_t mu2) {
-  const uint32_t v = L.a * c36 + L.b * c18 + L.c + cb;
+// Reference form of one residue (fp64_emu.cu:278-287): three 18-bit limbs,
+// 32-bit Barrett with one correction.  Exact whenever u < 2^56; kept for
+// elements beyond that (rows whose maximum is not finite), where the
+// reference's wrap-around arithmetic defines the bits.
+__device__ __forceinline__ uint32_t residue_ref(uint64_t u, uint32_t p, uint32_t c36, uint32_t c18, uint32_t cb,
+                                                uint32_t mu2) {
+  const uint32_t a = (uint32_t)(u >> 36), b = (uint32_t)((u >> 18) & 0x3FFFFu), c = (uint32_t)(u & 0x3FFFFu);
+  const uint32_t v = a * c36 + b * c18 + c + cb;
   const uint32_t q = __umulhi(v, mu2);
   uint32_t r = v - q * p;
   if (r >= p) r -= p;
@@ -76,11 +77,49 @@ __device__ __forceinline__ uint32_t residue_byte(const Limbs& L, uint32_t p, uin
   return (uint32_t)(uint8_t)(int8_t)rb;
 }
 
+// Fast form for u < 2^56: residue of (u + cb + h) from two dp4a over the
+// seven bytes of u, exact quotient by one umulhi; returns ((v + h) mod p) in
+// [0, p), the balanced residue plus h.
+__device__ __forceinline__ uint32_t residue_fast(uint32_t lo, uint32_t hi, uint32_t kl, uint32_t kh, uint32_t cbh,
+                                                 uint32_t mex, uint32_t p) {
+  const uint32_t v = __dp4a(lo, kl, __dp4a(hi, kh, cbh));
+  return v - __umulhi(v, mex) * p;
+}
+
 __device__ __forceinline__ uint32_t pack4(uint32_t b0, uint32_t b1, uint32_t b2, uint32_t b3) {
-  return b0 | (b1 << 8) | (b2 << 16) | (b3 << 24);
+  return __byte_perm(__byte_perm(b0, b1, 0x0040), __byte_perm(b2, b3, 0x0040), 0x5410);
 }
 __device__ __forceinline__ uint32_t pack4i(int b0, int b1, int b2, int b3) {
-  return pack4((uint32_t)(uint8_t)b0, (uint32_t)(uint8_t)b1, (uint32_t)(uint8_t)b2, (uint32_t)(uint8_t)b3);
+  return pack4((uint32_t)b0, (uint32_t)b1, (uint32_t)b2, (uint32_t)b3);
+}
+
+// Packed residue words (4 elements per word) of plane t for NE elements.
+template <int NE>
+__device__ __forceinline__ void residue_words(const Split (&S)[NE], bool fast, const ModTables& T, int t, int be,
+                                              uint32_t (&w)[NE / 4]) {
+  const uint32_t p = T.p[t];
+  const uint32_t cb = p - (uint32_t)T.pow2mod[t][be - 16];
+  if (fast) {
+    const uint32_t kl = T.kl[t], kh = T.kh[t], mex = T.mex[t], h = T.hh[t];
+    const uint32_t cbh = cb + h, h4 = h * 0x01010101u;
+#pragma unroll
+    for (int i = 0; i < NE / 4; i++) {
+      uint32_t r[4];
+#pragma unroll
+      for (int e = 0; e < 4; e++) {
+        const uint64_t u = S[4 * i + e].u;
+        r[e] = residue_fast((uint32_t)u, (uint32_t)(u >> 32), kl, kh, cbh, mex, p);
+      }
+      w[i] = __vsub4(pack4(r[0], r[1], r[2], r[3]), h4);
+    }
+  } else {
+    const uint32_t c36 = T.c36[t], c18 = T.c18[t], mu2 = T.mu2[t];
+#pragma unroll
+    for (int i = 0; i < NE / 4; i++)
+      w[i] = pack4(residue_ref(S[4 * i].u, p, c36, c18, cb, mu2), residue_ref(S[4 * i + 1].u, p, c36, c18, cb, mu2),
+                   residue_ref(S[4 * i + 2].u, p, c36, c18, cb, mu2),
+                   residue_ref(S[4 * i + 3].u, p, c36, c18, cb, mu2));
+  }
 }
 
 }  // namespace
@@ -114,24 +153,27 @@ __global__ void __launch_bounds__(256) extract_rows_kernel(const ExtractArgs a, 
 #pragma unroll
         for (int u = 0; u < 8; u++) x[u] = (k0 + u < a.K) ? __ldg(xr + k0 + u) : 0.0;
       }
-      Limbs L[8];
+      Split S[8];
+      bool ok = true;
 #pragma unroll
-      for (int u = 0; u < 8; u++) L[u] = split_elem(x[u], s, be, corr);
+      for (int u = 0; u < 8; u++) {
+        S[u] = split_elem(x[u], s, be, corr);
+        ok = ok && (S[u].u >> 56) == 0;
+      }
+      // The reference form only for chunks holding an element of a row with a
+      // non-finite maximum (u >= 2^56).
+      const bool fast = ok;
       int8_t* dst = a.planes + r * a.Kp + k0;
       for (int t = 0; t < P; t++) {
-        const uint32_t p = T.p[t], c36 = T.c36[t], c18 = T.c18[t], mu2 = T.mu2[t];
-        const uint32_t cb = p - (uint32_t)T.pow2mod[t][be - 16];
-        uint32_t by[8];
-#pragma unroll
-        for (int u = 0; u < 8; u++) by[u] = residue_byte(L[u], p, c36, c18, cb, mu2);
-        *reinterpret_cast<uint2*>(dst + t * pstride) =
-            make_uint2(pack4(by[0], by[1], by[2], by[3]), pack4(by[4], by[5], by[6], by[7]));
+        uint32_t w[2];
+        residue_words<8>(S, fast, T, t, be, w);
+        *reinterpret_cast<uint2*>(dst + t * pstride) = make_uint2(w[0], w[1]);
       }
       if (corr) {
         *reinterpret_cast<uint2*>(dst + a.hi_plane * pstride) =
-            make_uint2(pack4i(L[0].h, L[1].h, L[2].h, L[3].h), pack4i(L[4].h, L[5].h, L[6].h, L[7].h));
+            make_uint2(pack4i(S[0].h, S[1].h, S[2].h, S[3].h), pack4i(S[4].h, S[5].h, S[6].h, S[7].h));
         *reinterpret_cast<uint2*>(dst + a.q_plane * pstride) =
-            make_uint2(pack4i(L[0].q, L[1].q, L[2].q, L[3].q), pack4i(L[4].q, L[5].q, L[6].q, L[7].q));
+            make_uint2(pack4i(S[0].q, S[1].q, S[2].q, S[3].q), pack4i(S[4].q, S[5].q, S[6].q, S[7].q));
       }
     }
   }
@@ -161,22 +203,24 @@ __global__ void __launch_bounds__(256) extract_cols_kernel(const ExtractArgs a, 
   for (int qi = 0; qi < 2; qi++) {
     const int qd = ty + 8 * qi;
     const int64_t kb = k0 + 4 * qd;
-    Limbs L[4];
+    Split S[4];
+    bool ok = true;
 #pragma unroll
     for (int u = 0; u < 4; u++) {
       const int64_t k = kb + u;
       const double x = (nin && k < a.K) ? __ldg(xb + k * a.N) : 0.0;
-      L[u] = split_elem(x, s, be, corr);
+      S[u] = split_elem(x, s, be, corr);
+      ok = ok && (S[u].u >> 56) == 0;
     }
+    const bool fast = ok;
     for (int t = 0; t < P; t++) {
-      const uint32_t p = T.p[t], c36 = T.c36[t], c18 = T.c18[t], mu2 = T.mu2[t];
-      const uint32_t cb = p - (uint32_t)T.pow2mod[t][be - 16];
-      sw[t][tx][qd] = pack4(residue_byte(L[0], p, c36, c18, cb, mu2), residue_byte(L[1], p, c36, c18, cb, mu2),
-                            residue_byte(L[2], p, c36, c18, cb, mu2), residue_byte(L[3], p, c36, c18, cb, mu2));
+      uint32_t w[1];
+      residue_words<4>(S, fast, T, t, be, w);
+      sw[t][tx][qd] = w[0];
     }
     if (corr) {
-      sw[a.hi_plane][tx][qd] = pack4i(L[0].h, L[1].h, L[2].h, L[3].h);
-      sw[a.q_plane][tx][qd] = pack4i(L[0].q, L[1].q, L[2].q, L[3].q);
+      sw[a.hi_plane][tx][qd] = pack4i(S[0].h, S[1].h, S[2].h, S[3].h);
+      sw[a.q_plane][tx][qd] = pack4i(S[0].q, S[1].q, S[2].q, S[3].q);
     }
   }
   __syncthreads();

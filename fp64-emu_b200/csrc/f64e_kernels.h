@@ -16,8 +16,8 @@ namespace f64e {
 void launch_row_stats(const double* X, int64_t rows, int64_t cols, int bits, int16_t* sft, float* lg,
                       cudaStream_t s);
 void col_slabs(int64_t NF, int64_t K, int64_t* kslab, int* nslab);
-void launch_col_stats(const double* X, int64_t batch, int64_t K, int64_t N, int bits, int16_t* sft, float* lg,
-                      double* pmax, double* pss, cudaStream_t s);
+void launch_col_stats(const double* X, int64_t batch, int64_t K, int64_t N, int64_t kslab, int nslab, int bits,
+                      int16_t* sft, float* lg, double* pmax, double* pss, cudaStream_t s);
 void launch_maxlg(const float* lgA, int64_t m, const float* lgB, int64_t n, float* out, cudaStream_t s);
 
 // ---- extraction (f64e_extract.cu) ----

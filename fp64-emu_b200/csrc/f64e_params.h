@@ -24,6 +24,26 @@ struct ModTables {
   int32_t mp[kMaxP][kGroups];  // balanced (M_u mod p_t), u < t, four per word
   int32_t minv[kMaxP];         // (M_t mod p_t)^-1
   int64_t m64[2];              // products of moduli 0..6 and 7..13
+
+  // Fast forms (exact quotients, no correction steps).  Extraction: the
+  // residue pre-sum of a biased integer u < 2^56 is two dp4a over its seven
+  // bytes with the weights 2^(8i) mod p; its quotient by p is umulhi(v, mex)
+  // exactly for v < 2^24.  The balanced residue is ((v + h) mod p) - h with
+  // h = floor(p / 2).
+  uint32_t kl[kMaxP];          // bytes 2^0, 2^8, 2^16, 2^24 mod p
+  uint32_t kh[kMaxP];          // bytes 2^32, 2^40, 2^48 mod p (top byte 0)
+  uint32_t mex[kMaxP];         // ceil(2^32 / p)
+  uint32_t hh[kMaxP];          // floor(p / 2)
+  // Reconstruction with digits stored offset, d' = d + h in [0, p): the
+  // Garner sum uses unsigned factors cu = M_u mod p_t, and the offset terms
+  // fold into one constant per digit, krec = ((sum_u h_u cu) * minv + h_t)
+  // mod p_t plus a multiple of p_t >= 2^29 keeping the argument positive;
+  // the quotient is (umulhi(X, mrec) >> 7) exactly for X < 2^31 (p > 128).
+  uint32_t cu[kMaxP][kGroups]; // unsigned (M_u mod p_t), u < t, four per word
+  uint32_t krec[kMaxP];
+  uint32_t mrec[kMaxP];        // ceil(2^39 / p)
+  int64_t hoff[3];             // Horner value of the offsets h per 7-modulus group
+  int fast_recon;              // every modulus > 128
 };
 
 // Device-resident scalars at the head of every workspace.  maxlg holds the

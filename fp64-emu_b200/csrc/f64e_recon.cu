@@ -18,21 +18,68 @@ namespace f64e {
 
 namespace {
 
-// Correctly rounded (RNE) conversion of a signed 128-bit integer.
-__device__ __forceinline__ double i128_to_double(__int128 v) {
-  const bool neg = v < 0;
-  const unsigned __int128 u = neg ? (unsigned __int128)0 - (unsigned __int128)v : (unsigned __int128)v;
-  const uint64_t hi = (uint64_t)(u >> 64), lo = (uint64_t)u;
+// x * 2^e, exact: adds to the exponent field when the result stays normal,
+// otherwise defers to ldexp (subnormal / overflow / zero), so the bits are
+// ldexp's in every case.
+__device__ __forceinline__ double scale2(double x, int e) {
+  const uint64_t b = (uint64_t)__double_as_longlong(x);
+  const int ex = (int)((b >> 52) & 0x7FF);
+  const int ne = ex + e;
+  if (ex != 0 && ex != 0x7FF && ne > 0 && ne < 0x7FF)
+    return __longlong_as_double((long long)(b + ((uint64_t)(int64_t)e << 52)));
+  return ldexp(x, e);
+}
+
+// Signed 128-bit integer as two 64-bit halves.
+struct I128 {
+  uint64_t lo;
+  int64_t hi;
+};
+
+__device__ __forceinline__ I128 i128_of(int64_t v) {
+  I128 r;
+  r.lo = (uint64_t)v;
+  r.hi = v >> 63;
+  return r;
+}
+
+// a * m + d for 0 < m < 2^63 (a group product of moduli), signed d.
+__device__ __forceinline__ I128 i128_mul_add(I128 a, uint64_t m, int64_t d) {
+  const uint64_t lo = a.lo * m;
+  const uint64_t hi = __umul64hi(a.lo, m) + (uint64_t)a.hi * m;
+  I128 r;
+  r.lo = lo + (uint64_t)d;
+  r.hi = (int64_t)(hi + (r.lo < lo ? 1ULL : 0ULL) + (d < 0 ? ~0ULL : 0ULL));
+  return r;
+}
+
+// a + c * 2^s for 0 < s < 64.
+__device__ __forceinline__ I128 i128_add_shl(I128 a, int64_t c, int s) {
+  const uint64_t clo = (uint64_t)c << s;
+  const uint64_t chi = (uint64_t)(c >> (64 - s));
+  I128 r;
+  r.lo = a.lo + clo;
+  r.hi = (int64_t)((uint64_t)a.hi + chi + (r.lo < clo ? 1ULL : 0ULL));
+  return r;
+}
+
+// Correctly rounded (RNE) conversion: keep the top 64 significant bits, fold
+// the dropped tail into a sticky bit far below the rounding position.
+__device__ __forceinline__ double i128_to_double(I128 v) {
+  const bool neg = v.hi < 0;
+  uint64_t lo = v.lo, hi = (uint64_t)v.hi;
+  if (neg) {
+    lo = ~lo + 1ULL;
+    hi = ~hi + (lo == 0ULL ? 1ULL : 0ULL);
+  }
   double m;
   if (hi == 0) {
     m = __ull2double_rn(lo);
   } else {
-    // Keep the top 64 significant bits; fold the dropped tail into a sticky
-    // bit far below the rounding position.
     const int sh = 64 - __clzll((long long)hi);  // 1..64
     const uint64_t top = (sh == 64) ? hi : ((hi << (64 - sh)) | (lo >> sh));
     const uint64_t tail = (sh == 64) ? lo : (lo & ((1ULL << sh) - 1ULL));
-    m = ldexp(__ull2double_rn(top | (tail ? 1ULL : 0ULL)), sh);
+    m = scale2(__ull2double_rn(top | (tail ? 1ULL : 0ULL)), sh);
   }
   return neg ? -m : m;
 }
@@ -60,6 +107,7 @@ __device__ __forceinline__ void load_corr(const ReconArgs& a, int64_t off, int64
 
 }  // namespace
 
+// General form (any moduli): balanced digits, reduction with one correction.
 // Block (64, 4): x spans 64 four-column chunks of a row, y four rows.
 template <int CM>
 __global__ void __launch_bounds__(256) reconstruct_kernel(const ReconArgs a, const ModTables T) {
@@ -116,11 +164,97 @@ __global__ void __launch_bounds__(256) reconstruct_kernel(const ReconArgs a, con
         const int64_t j = j0 + e;
         const int sh = -sa - (j < a.N ? (int)sB[j] + gn.g : 0);
         if (a.exact) {
-          __int128 v = (ng == 3) ? (__int128)a2 : ((ng == 2) ? (__int128)a1 : (__int128)a0);
-          if (ng == 3) v = v * (__int128)T.m64[1] + a1;
-          if (ng >= 2) v = v * (__int128)T.m64[0] + a0;
-          v += (__int128)cr[e] * ((__int128)1 << cshift);
-          outv[e] = ldexp(i128_to_double(v), sh);
+          I128 v = i128_of(ng == 3 ? a2 : (ng == 2 ? a1 : a0));
+          if (ng == 3) v = i128_mul_add(v, (uint64_t)T.m64[1], a1);
+          if (ng >= 2) v = i128_mul_add(v, (uint64_t)T.m64[0], a0);
+          v = i128_add_shl(v, cr[e], cshift);
+          outv[e] = scale2(i128_to_double(v), sh);
+        } else {
+          double v = (double)((ng == 3) ? a2 : ((ng == 2) ? a1 : a0));
+          if (ng == 3) v = fma(v, (double)T.m64[1], (double)a1);
+          if (ng >= 2) v = fma(v, (double)T.m64[0], (double)a0);
+          v += ldexp((double)cr[e], cshift);
+          outv[e] = ldexp(v, sh);
+        }
+      }
+      double* crow = a.C + i * a.N;
+      if (vec_out && j0 + 4 <= a.N) {
+        *reinterpret_cast<double2*>(crow + j0) = make_double2(outv[0], outv[1]);
+        *reinterpret_cast<double2*>(crow + j0 + 2) = make_double2(outv[2], outv[3]);
+      } else {
+#pragma unroll
+        for (int e = 0; e < 4; e++)
+          if (j0 + e < a.N) crow[j0 + e] = outv[e];
+      }
+    }
+  }
+}
+
+// Fast form (every modulus > 128): digits kept offset, d' = d + h in [0, p),
+// exact quotients, no correction steps (constants: ModTables fast forms).
+template <int CM>
+__global__ void __launch_bounds__(256) reconstruct_fast_kernel(const ReconArgs a, const ModTables T) {
+  const Gain gn = pick_gain(a.maxlg[0], a.maxlg[1], T.log2M, a.bits);
+  const int cshift = gn.bits_eff - 15;
+  const int P = T.P;
+  const int ng = (P + 6) / 7;
+  const int64_t nq = (a.N + 3) >> 2;
+  const int64_t plane = a.MF * a.ldn;
+  const bool vec_out = ((a.N & 3) == 0) && ((reinterpret_cast<uintptr_t>(a.C) & 15) == 0);
+  for (int64_t i = (int64_t)blockIdx.y * 4 + threadIdx.y; i < a.MF; i += (int64_t)gridDim.y * 4) {
+    const int sa = (int)a.sftA[i] + gn.g;
+    const int16_t* __restrict__ sB = a.sftB + (i / a.M) * a.N;
+    for (int64_t jq = (int64_t)blockIdx.x * 64 + threadIdx.x; jq < nq; jq += (int64_t)gridDim.x * 64) {
+      const int64_t j0 = jq << 2;
+      const int64_t off = i * a.ldn + j0;
+      uint32_t rw[kMaxP];
+#pragma unroll
+      for (int t = 0; t < kMaxP; t++)
+        rw[t] = (t < P) ? __ldg(reinterpret_cast<const unsigned int*>(a.res + t * plane + off)) : 0u;
+      int64_t cr[4];
+      load_corr<CM>(a, off, plane, cr);
+      uint32_t dp[4][kGroups];
+#pragma unroll
+      for (int e = 0; e < 4; e++)
+#pragma unroll
+        for (int g = 0; g < kGroups; g++) dp[e][g] = 0;
+#pragma unroll
+      for (int t = 0; t < kMaxP; t++) {
+        if (t >= P) break;
+        const uint32_t p = T.p[t], mr = T.mrec[t], kr = T.krec[t];
+        const int mi = T.minv[t];
+#pragma unroll
+        for (int e = 0; e < 4; e++) {
+          const int rt = (int)(int8_t)(uint8_t)(rw[t] >> (8 * e));
+          uint32_t acc = 0;
+#pragma unroll
+          for (int g = 0; g < (t + 3) / 4; g++) acc = __dp4a(dp[e][g], T.cu[t][g], acc);
+          const uint32_t X = (uint32_t)((rt - (int)acc) * mi) + kr;   // in [0, 2^31)
+          const uint32_t d = X - (__umulhi(X, mr) >> 7) * p;          // d + h in [0, p)
+          dp[e][t >> 2] |= d << (8 * (t & 3));
+        }
+      }
+      double outv[4];
+#pragma unroll
+      for (int e = 0; e < 4; e++) {
+        uint64_t g0 = 0, g1 = 0, g2 = 0;
+#pragma unroll
+        for (int t = kMaxP - 1; t >= 0; t--) {
+          if (t >= P) continue;
+          const uint64_t d = (dp[e][t >> 2] >> (8 * (t & 3))) & 0xFFu;
+          if (t >= 14) g2 = g2 * T.p[t] + d;
+          else if (t >= 7) g1 = g1 * T.p[t] + d;
+          else g0 = g0 * T.p[t] + d;
+        }
+        const int64_t a0 = (int64_t)g0 - T.hoff[0], a1 = (int64_t)g1 - T.hoff[1], a2 = (int64_t)g2 - T.hoff[2];
+        const int64_t j = j0 + e;
+        const int sh = -sa - (j < a.N ? (int)sB[j] + gn.g : 0);
+        if (a.exact) {
+          I128 v = i128_of(ng == 3 ? a2 : (ng == 2 ? a1 : a0));
+          if (ng == 3) v = i128_mul_add(v, (uint64_t)T.m64[1], a1);
+          if (ng >= 2) v = i128_mul_add(v, (uint64_t)T.m64[0], a0);
+          if (CM != 0) v = i128_add_shl(v, cr[e], cshift);
+          outv[e] = scale2(i128_to_double(v), sh);
         } else {
           double v = (double)((ng == 3) ? a2 : ((ng == 2) ? a1 : a0));
           if (ng == 3) v = fma(v, (double)T.m64[1], (double)a1);
@@ -148,6 +282,15 @@ void launch_reconstruct(const ReconArgs& a, const ModTables& T, cudaStream_t s) 
   const dim3 grid((unsigned)std::min<int64_t>((nq + 63) / 64, 1 << 20),
                   (unsigned)std::min<int64_t>((a.MF + 3) / 4, 65535));
   const dim3 block(64, 4);
+  if (T.fast_recon) {
+    switch (a.corr_mode) {
+      case 0: reconstruct_fast_kernel<0><<<grid, block, 0, s>>>(a, T); break;
+      case 1: reconstruct_fast_kernel<1><<<grid, block, 0, s>>>(a, T); break;
+      case 2: reconstruct_fast_kernel<2><<<grid, block, 0, s>>>(a, T); break;
+      default: reconstruct_fast_kernel<3><<<grid, block, 0, s>>>(a, T); break;
+    }
+    return;
+  }
   switch (a.corr_mode) {
     case 0: reconstruct_kernel<0><<<grid, block, 0, s>>>(a, T); break;
     case 1: reconstruct_kernel<1><<<grid, block, 0, s>>>(a, T); break;

@@ -170,13 +170,10 @@ void col_slabs(int64_t NF, int64_t K, int64_t* kslab, int* nslab) {
   *nslab = *kslab > 0 ? (int)((K + *kslab - 1) / *kslab) : 0;
 }
 
-void launch_col_stats(const double* X, int64_t batch, int64_t K, int64_t N, int bits, int16_t* sft, float* lg,
-                      double* pmax, double* pss, cudaStream_t s) {
+void launch_col_stats(const double* X, int64_t batch, int64_t K, int64_t N, int64_t kslab, int nslab, int bits,
+                      int16_t* sft, float* lg, double* pmax, double* pss, cudaStream_t s) {
   const int64_t NF = batch * N;
   if (NF <= 0) return;
-  int64_t kslab;
-  int nslab;
-  col_slabs(NF, K, &kslab, &nslab);
   const unsigned gx = (unsigned)((NF + 255) / 256);
   if (nslab > 0) col_partial_kernel<<<dim3(gx, nslab), 256, 0, s>>>(X, NF, K, N, kslab, pmax, pss);
   col_finalize_kernel<<<gx, 256, 0, s>>>(pmax, pss, NF, nslab, bits, sft, lg);

@@ -50,6 +50,7 @@ f64e_problem problem(int64_t batch, int64_t M, int64_t N, int64_t K, bool b_kn, 
   p.exact = exact ? 1 : 0;
   p.bits = (int32_t)bits;
   p.use_corr = use_corr ? 1 : 0;
+  p.slab_cols = 0;
   return p;
 }
 
@@ -188,9 +189,10 @@ f64e_problem problem_of(const at::Tensor& A, const at::Tensor& B, bool b_kn, con
 }
 
 int64_t workspace_bytes(const at::Tensor& A, const at::Tensor& B, const at::Tensor& primes_cpu, bool b_kn,
-                        bool use_corr) {
+                        bool use_corr, int64_t slab_cols) {
   const auto pr = host_primes(primes_cpu);
-  const f64e_problem p = problem_of(A, B, b_kn, pr, true, 53, use_corr);
+  f64e_problem p = problem_of(A, B, b_kn, pr, true, 53, use_corr);
+  p.slab_cols = slab_cols;
   const size_t n = f64e_workspace_size(&p);
   TORCH_CHECK(n > 0, "fp64_emu: ", f64e_last_error());
   return (int64_t)n;
@@ -198,13 +200,14 @@ int64_t workspace_bytes(const at::Tensor& A, const at::Tensor& B, const at::Tens
 
 void gemm_phase(at::Tensor& out, at::Tensor& ws, const at::Tensor& A, const at::Tensor& B,
                 const at::Tensor& primes_cpu, bool b_kn, bool exact, int64_t bits, bool use_corr, int64_t phases,
-                bool checked) {
+                bool checked, int64_t slab_cols) {
   TORCH_CHECK(A.is_cuda() && B.is_cuda() && A.dtype() == at::kDouble && B.dtype() == at::kDouble,
               "A,B must be f64 CUDA");
   TORCH_CHECK(A.is_contiguous() && B.is_contiguous() && out.is_contiguous() && ws.is_contiguous(), "contig");
   TORCH_CHECK(ws.is_cuda() && ws.device() == A.device() && out.device() == A.device(), "same device");
   const auto pr = host_primes(primes_cpu);
-  const f64e_problem p = problem_of(A, B, b_kn, pr, exact, bits, use_corr);
+  f64e_problem p = problem_of(A, B, b_kn, pr, exact, bits, use_corr);
+  p.slab_cols = slab_cols;
   TORCH_CHECK(out.dtype() == at::kDouble && out.numel() == p.batch * p.M * p.N, "out f64 of batch*M*N");
   const c10::cuda::CUDAGuard guard(A.device());
   const size_t nb = (size_t)ws.numel() * ws.element_size();
@@ -217,13 +220,14 @@ void gemm_phase(at::Tensor& out, at::Tensor& ws, const at::Tensor& A, const at::
 }
 
 void gemm_ws(at::Tensor& out, at::Tensor& ws, const at::Tensor& A, const at::Tensor& B,
-             const at::Tensor& primes_cpu, bool b_kn, bool exact, int64_t bits, bool use_corr, int64_t phases) {
-  gemm_phase(out, ws, A, B, primes_cpu, b_kn, exact, bits, use_corr, phases, false);
+             const at::Tensor& primes_cpu, bool b_kn, bool exact, int64_t bits, bool use_corr, int64_t phases,
+             int64_t slab_cols) {
+  gemm_phase(out, ws, A, B, primes_cpu, b_kn, exact, bits, use_corr, phases, false, slab_cols);
 }
 
 void gemm_checked(at::Tensor& out, at::Tensor& ws, const at::Tensor& A, const at::Tensor& B,
                   const at::Tensor& primes_cpu, bool b_kn, bool exact, int64_t bits, bool use_corr) {
-  gemm_phase(out, ws, A, B, primes_cpu, b_kn, exact, bits, use_corr, F64E_PHASE_ALL, true);
+  gemm_phase(out, ws, A, B, primes_cpu, b_kn, exact, bits, use_corr, F64E_PHASE_ALL, true, 0);
 }
 
 int64_t status(const at::Tensor& ws) {
@@ -267,10 +271,12 @@ TORCH_LIBRARY(fp64_emu_b200, ops) {
   ops.def(
       "fp64_emu_mm_timed(Tensor! out, Tensor! times, Tensor A, Tensor B, Tensor primes_cpu, Tensor inv_cpu, Tensor "
       "mu_cpu, bool exact, int bits=53, bool use_corr=True) -> ()");
-  ops.def("fp64_emu_workspace_bytes(Tensor A, Tensor B, Tensor primes_cpu, bool b_kn, bool use_corr) -> int");
+  ops.def(
+      "fp64_emu_workspace_bytes(Tensor A, Tensor B, Tensor primes_cpu, bool b_kn, bool use_corr, int slab_cols=0) "
+      "-> int");
   ops.def(
       "fp64_emu_gemm_ws(Tensor! out, Tensor! ws, Tensor A, Tensor B, Tensor primes_cpu, bool b_kn, bool exact, "
-      "int bits, bool use_corr, int phases) -> ()");
+      "int bits, bool use_corr, int phases, int slab_cols=0) -> ()");
   ops.def(
       "fp64_emu_gemm_checked(Tensor! out, Tensor! ws, Tensor A, Tensor B, Tensor primes_cpu, bool b_kn, bool "
       "exact, int bits, bool use_corr) -> ()");

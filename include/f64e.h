@@ -54,11 +54,24 @@ enum {
   F64E_B_KN = 1  /* B is [batch, K, N]: mm_nt, bmm_nt (out = A @ B) */
 };
 
-/* Phases of f64e_gemm: sizing computes the per-row / per-column shifts and the
- * two operand maxima of the log2 norms (float[2] at workspace offset 0); a
- * partitioned multi-GPU caller MAX-all-reduces those two floats between the
- * phases so every rank uses the single-GPU operand width. */
-enum { F64E_PHASE_SIZING = 1, F64E_PHASE_COMPUTE = 2, F64E_PHASE_ALL = 3 };
+/* Phases of f64e_gemm, run in this order on the caller's stream:
+ *   SIZING   per-row / per-column shifts and the two operand maxima of the
+ *            log2 norms (float[2] at workspace offset 0);
+ *   EXTRACT  residue and correction planes;
+ *   GEMM     the modular tensor-core GEMMs;
+ *   RECON    reconstruction into out.
+ * A partitioned multi-GPU caller MAX-all-reduces the two floats between
+ * SIZING and the rest, so every rank uses the single-GPU operand width.
+ * Deep-K problems (K > 131071) interleave EXTRACT and GEMM per segment and
+ * need both bits in the same call. */
+enum {
+  F64E_PHASE_SIZING = 1,
+  F64E_PHASE_EXTRACT = 2,
+  F64E_PHASE_GEMM = 4,
+  F64E_PHASE_RECON = 8,
+  F64E_PHASE_COMPUTE = 14,
+  F64E_PHASE_ALL = 15
+};
 
 /* Largest modulus count (reference: fp64_emu_maxp, fp64_emu.cu:956). */
 F64E_API int64_t f64e_maxp(void);
@@ -73,6 +86,10 @@ typedef struct f64e_problem {
   int32_t exact;         /* int128 recombine (1) or fp64 recombine (0) */
   int32_t bits;          /* operand width before widening, 16..53 */
   int32_t use_corr;      /* the two first-order correction GEMMs */
+  int64_t slab_cols;     /* F64E_B_KN only: column count whose slab rule orders the
+                            column sums (fp64_emu.cu:1159-1162); 0 = batch * N.  A
+                            rank holding a slice of the columns passes the full
+                            count to reproduce the single-GPU sums exactly. */
 } f64e_problem;
 
 /* Bytes of workspace the problem needs (0 when the arguments are invalid;

@@ -30,6 +30,20 @@ __device__ __forceinline__ uint64_t rne_shr(uint64_t mag, int s) {
   return keep + ((rem > half || (rem == half && (keep & 1ULL))) ? 1ULL : 0ULL);
 }
 
+// Same value as rne_shr for v < 2^62: adding 2^(s-1) - 1 plus the kept
+// low bit carries into the kept part exactly when the dropped part is above
+// half, or equal to half with an odd kept part.
+__device__ __forceinline__ uint64_t rne_shr_small(uint64_t v, int s) {
+  if (s <= 0) return (-s < 64) ? (v << (-s)) : 0ULL;
+  if (s > 63) return 0ULL;
+  const uint64_t lsb = (v >> s) & 1ULL;
+  return (v + ((1ULL << (s - 1)) - 1ULL) + lsb) >> s;
+}
+
+// Out-of-line copy for the rare wide operand (rows whose maximum is not
+// finite), so the common path is not predicated through it.
+__device__ __noinline__ uint64_t rne_shr_wide(uint64_t v, int s) { return rne_shr(v, s); }
+
 __device__ __forceinline__ int clamp127(int64_t v) { return v > 127 ? 127 : (v < -127 ? -127 : (int)v); }
 
 // Biased scaled integer u = T*sign + 2^b (two's complement, mod 2^64) and
@@ -46,12 +60,12 @@ __device__ __forceinline__ Split split_elem(double x, int s, int be, bool corr) 
   const uint64_t m = xb & 0xFFFFFFFFFFFFFULL;
   const uint64_t mag = e ? ((1ULL << 52) | m) : m;
   const int t = (e ? e : 1) - 1075 + s + 52;
-  const uint64_t Tu = rne_shr(mag, 52 - t);
+  const uint64_t Tu = rne_shr_small(mag, 52 - t);  // mag < 2^53
   const uint64_t td = neg ? (0ULL - Tu) : Tu;  // two's complement of the signed value
   Split S;
   if (corr) {
-    const uint64_t r8 = rne_shr(mag, 44 - t) - (Tu << 8);
-    const uint64_t h8 = rne_shr(Tu, be - 7);
+    const uint64_t r8 = rne_shr_small(mag, 44 - t) - (Tu << 8);
+    const uint64_t h8 = (Tu >> 62) ? rne_shr_wide(Tu, be - 7) : rne_shr_small(Tu, be - 7);
     S.h = clamp127((int64_t)(neg ? (0ULL - h8) : h8));
     S.q = clamp127((int64_t)(neg ? (0ULL - r8) : r8));
   } else {
@@ -77,13 +91,14 @@ __device__ __forceinline__ uint32_t residue_ref(uint64_t u, uint32_t p, uint32_t
   return (uint32_t)(uint8_t)(int8_t)rb;
 }
 
-// Fast form for u < 2^56: residue of (u + cb + h) from two dp4a over the
-// seven bytes of u, exact quotient by one umulhi; returns ((v + h) mod p) in
-// [0, p), the balanced residue plus h.
-__device__ __forceinline__ uint32_t residue_fast(uint32_t lo, uint32_t hi, uint32_t kl, uint32_t kh, uint32_t cbh,
-                                                 uint32_t mex, uint32_t p) {
-  const uint32_t v = __dp4a(lo, kl, __dp4a(hi, kh, cbh));
-  return v - __umulhi(v, mex) * p;
+// Fast form for u < 2^56: v = (u + cb) folded to under 2^19 by two dp4a over
+// the seven bytes of u; q = floor((v + h) / p) is the high word of
+// v * mex + h * mex exactly (v + h < 2^24); v - q p is the balanced residue.
+__device__ __forceinline__ uint32_t residue_fast(uint32_t lo, uint32_t hi, uint32_t kl, uint32_t kh, uint32_t cb,
+                                                 uint32_t mex, uint64_t hm, uint32_t p) {
+  const uint32_t v = __dp4a(lo, kl, __dp4a(hi, kh, cb));
+  const uint32_t q = (uint32_t)(((uint64_t)v * mex + hm) >> 32);
+  return v - q * p;
 }
 
 __device__ __forceinline__ uint32_t pack4(uint32_t b0, uint32_t b1, uint32_t b2, uint32_t b3) {
@@ -93,33 +108,33 @@ __device__ __forceinline__ uint32_t pack4i(int b0, int b1, int b2, int b3) {
   return pack4((uint32_t)b0, (uint32_t)b1, (uint32_t)b2, (uint32_t)b3);
 }
 
-// Packed residue words (4 elements per word) of plane t for NE elements.
+// Packed residue words (4 elements per word) of plane t, fast form.
 template <int NE>
-__device__ __forceinline__ void residue_words(const Split (&S)[NE], bool fast, const ModTables& T, int t, int be,
+__device__ __forceinline__ void residue_words(const Split (&S)[NE], const ModTables& T, int t, int be,
                                               uint32_t (&w)[NE / 4]) {
   const uint32_t p = T.p[t];
   const uint32_t cb = p - (uint32_t)T.pow2mod[t][be - 16];
-  if (fast) {
-    const uint32_t kl = T.kl[t], kh = T.kh[t], mex = T.mex[t], h = T.hh[t];
-    const uint32_t cbh = cb + h, h4 = h * 0x01010101u;
+  const uint32_t kl = T.kl[t], kh = T.kh[t], mex = T.mex[t];
+  const uint64_t hm = (uint64_t)T.hh[t] * mex;
 #pragma unroll
-    for (int i = 0; i < NE / 4; i++) {
-      uint32_t r[4];
+  for (int i = 0; i < NE / 4; i++) {
+    uint32_t r[4];
 #pragma unroll
-      for (int e = 0; e < 4; e++) {
-        const uint64_t u = S[4 * i + e].u;
-        r[e] = residue_fast((uint32_t)u, (uint32_t)(u >> 32), kl, kh, cbh, mex, p);
-      }
-      w[i] = __vsub4(pack4(r[0], r[1], r[2], r[3]), h4);
+    for (int e = 0; e < 4; e++) {
+      const uint64_t u = S[4 * i + e].u;
+      r[e] = residue_fast((uint32_t)u, (uint32_t)(u >> 32), kl, kh, cb, mex, hm, p);
     }
-  } else {
-    const uint32_t c36 = T.c36[t], c18 = T.c18[t], mu2 = T.mu2[t];
-#pragma unroll
-    for (int i = 0; i < NE / 4; i++)
-      w[i] = pack4(residue_ref(S[4 * i].u, p, c36, c18, cb, mu2), residue_ref(S[4 * i + 1].u, p, c36, c18, cb, mu2),
-                   residue_ref(S[4 * i + 2].u, p, c36, c18, cb, mu2),
-                   residue_ref(S[4 * i + 3].u, p, c36, c18, cb, mu2));
+    w[i] = pack4(r[0], r[1], r[2], r[3]);
   }
+}
+
+// Reference form for one 4-element word of plane t (rare: elements of rows
+// whose maximum is not finite).  Out of line, so the fast path is not
+// predicated through it.
+__device__ __noinline__ uint32_t residue_word_ref(uint64_t u0, uint64_t u1, uint64_t u2, uint64_t u3, uint32_t p,
+                                                  uint32_t c36, uint32_t c18, uint32_t cb, uint32_t mu2) {
+  return pack4(residue_ref(u0, p, c36, c18, cb, mu2), residue_ref(u1, p, c36, c18, cb, mu2),
+               residue_ref(u2, p, c36, c18, cb, mu2), residue_ref(u3, p, c36, c18, cb, mu2));
 }
 
 }  // namespace
@@ -162,12 +177,22 @@ __global__ void __launch_bounds__(256) extract_rows_kernel(const ExtractArgs a, 
       }
       // The reference form only for chunks holding an element of a row with a
       // non-finite maximum (u >= 2^56).
-      const bool fast = ok;
       int8_t* dst = a.planes + r * a.Kp + k0;
-      for (int t = 0; t < P; t++) {
-        uint32_t w[2];
-        residue_words<8>(S, fast, T, t, be, w);
-        *reinterpret_cast<uint2*>(dst + t * pstride) = make_uint2(w[0], w[1]);
+      if (ok) {
+#pragma unroll
+        for (int t = 0; t < kMaxP; t++) {
+          if (t >= P) break;
+          uint32_t w[2];
+          residue_words<8>(S, T, t, be, w);
+          *reinterpret_cast<uint2*>(dst + t * pstride) = make_uint2(w[0], w[1]);
+        }
+      } else {
+        for (int t = 0; t < P; t++) {
+          const uint32_t p = T.p[t], cb = p - (uint32_t)T.pow2mod[t][be - 16];
+          *reinterpret_cast<uint2*>(dst + t * pstride) =
+              make_uint2(residue_word_ref(S[0].u, S[1].u, S[2].u, S[3].u, p, T.c36[t], T.c18[t], cb, T.mu2[t]),
+                         residue_word_ref(S[4].u, S[5].u, S[6].u, S[7].u, p, T.c36[t], T.c18[t], cb, T.mu2[t]));
+        }
       }
       if (corr) {
         *reinterpret_cast<uint2*>(dst + a.hi_plane * pstride) =
@@ -212,11 +237,19 @@ __global__ void __launch_bounds__(256) extract_cols_kernel(const ExtractArgs a, 
       S[u] = split_elem(x, s, be, corr);
       ok = ok && (S[u].u >> 56) == 0;
     }
-    const bool fast = ok;
-    for (int t = 0; t < P; t++) {
-      uint32_t w[1];
-      residue_words<4>(S, fast, T, t, be, w);
-      sw[t][tx][qd] = w[0];
+    if (ok) {
+#pragma unroll
+      for (int t = 0; t < kMaxP; t++) {
+        if (t >= P) break;
+        uint32_t w[1];
+        residue_words<4>(S, T, t, be, w);
+        sw[t][tx][qd] = w[0];
+      }
+    } else {
+      for (int t = 0; t < P; t++) {
+        const uint32_t p = T.p[t], cb = p - (uint32_t)T.pow2mod[t][be - 16];
+        sw[t][tx][qd] = residue_word_ref(S[0].u, S[1].u, S[2].u, S[3].u, p, T.c36[t], T.c18[t], cb, T.mu2[t]);
+      }
     }
     if (corr) {
       sw[a.hi_plane][tx][qd] = pack4i(S[0].h, S[1].h, S[2].h, S[3].h);

@@ -21,13 +21,15 @@ namespace {
 // x * 2^e, exact: adds to the exponent field when the result stays normal,
 // otherwise defers to ldexp (subnormal / overflow / zero), so the bits are
 // ldexp's in every case.
+__device__ __noinline__ double ldexp_slow(double x, int e) { return ldexp(x, e); }
+
 __device__ __forceinline__ double scale2(double x, int e) {
   const uint64_t b = (uint64_t)__double_as_longlong(x);
   const int ex = (int)((b >> 52) & 0x7FF);
   const int ne = ex + e;
   if (ex != 0 && ex != 0x7FF && ne > 0 && ne < 0x7FF)
     return __longlong_as_double((long long)(b + ((uint64_t)(int64_t)e << 52)));
-  return ldexp(x, e);
+  return ldexp_slow(x, e);  // zero, subnormal or overflowing results: ldexp's rounding
 }
 
 // Signed 128-bit integer as two 64-bit halves.
@@ -51,6 +53,38 @@ __device__ __forceinline__ I128 i128_mul_add(I128 a, uint64_t m, int64_t d) {
   r.lo = lo + (uint64_t)d;
   r.hi = (int64_t)(hi + (r.lo < lo ? 1ULL : 0ULL) + (d < 0 ? ~0ULL : 0ULL));
   return r;
+}
+
+// a * m + d for signed 64-bit a, 0 < m < 2^63, signed d: the sign of a
+// contributes -m to the high word instead of a full second product.
+__device__ __forceinline__ I128 i128_mul_add_s64(int64_t a, uint64_t m, int64_t d) {
+  const uint64_t au = (uint64_t)a;
+  const uint64_t lo = au * m;
+  uint64_t hi = __umul64hi(au, m) - (a < 0 ? m : 0ULL);
+  I128 r;
+  r.lo = lo + (uint64_t)d;
+  r.hi = (int64_t)(hi + (r.lo < lo ? 1ULL : 0ULL) + (d < 0 ? ~0ULL : 0ULL));
+  return r;
+}
+
+// Horner value of the offset digits t = lo .. hi of one group (hi - lo <= 6):
+// the first three steps stay below 2^32, the rest run in 64 bits.
+template <int LO, int HI>
+__device__ __forceinline__ uint64_t horner_group(const uint32_t (&dp)[kGroups], const ModTables& T, int P) {
+  uint32_t g32 = 0;
+  uint64_t g64 = 0;
+  int steps = 0;
+#pragma unroll
+  for (int t = HI; t >= LO; t--) {
+    if (t >= P) continue;
+    const uint32_t d = __byte_perm(dp[t >> 2], 0u, 0x4440u | (uint32_t)(t & 3));
+    if (steps == 0) g32 = d;
+    else if (steps < 4) g32 = g32 * T.p[t] + d;
+    else if (steps == 4) g64 = (uint64_t)g32 * T.p[t] + d;
+    else g64 = g64 * T.p[t] + d;
+    steps++;
+  }
+  return steps <= 4 ? (uint64_t)g32 : g64;
 }
 
 // a + c * 2^s for 0 < s < 64.
@@ -190,10 +224,15 @@ __global__ void __launch_bounds__(256) reconstruct_kernel(const ReconArgs a, con
   }
 }
 
+// byte_perm selector writing the low byte of the second operand into byte k.
+__host__ __device__ constexpr uint32_t insert_sel(int k) {
+  return (0x3210u & ~(0xFu << (4 * k))) | (4u << (4 * k));
+}
+
 // Fast form (every modulus > 128): digits kept offset, d' = d + h in [0, p),
 // exact quotients, no correction steps (constants: ModTables fast forms).
-template <int CM>
-__global__ void __launch_bounds__(256) reconstruct_fast_kernel(const ReconArgs a, const ModTables T) {
+template <int CM, bool EXACT>
+__global__ void __launch_bounds__(256, 2) reconstruct_fast_kernel(const ReconArgs a, const ModTables T) {
   const Gain gn = pick_gain(a.maxlg[0], a.maxlg[1], T.log2M, a.bits);
   const int cshift = gn.bits_eff - 15;
   const int P = T.P;
@@ -231,28 +270,27 @@ __global__ void __launch_bounds__(256) reconstruct_fast_kernel(const ReconArgs a
           for (int g = 0; g < (t + 3) / 4; g++) acc = __dp4a(dp[e][g], T.cu[t][g], acc);
           const uint32_t X = (uint32_t)((rt - (int)acc) * mi) + kr;   // in [0, 2^31)
           const uint32_t d = X - (__umulhi(X, mr) >> 7) * p;          // d + h in [0, p)
-          dp[e][t >> 2] |= d << (8 * (t & 3));
+          dp[e][t >> 2] = __byte_perm(dp[e][t >> 2], d, insert_sel(t & 3));
         }
       }
       double outv[4];
 #pragma unroll
       for (int e = 0; e < 4; e++) {
-        uint64_t g0 = 0, g1 = 0, g2 = 0;
-#pragma unroll
-        for (int t = kMaxP - 1; t >= 0; t--) {
-          if (t >= P) continue;
-          const uint64_t d = (dp[e][t >> 2] >> (8 * (t & 3))) & 0xFFu;
-          if (t >= 14) g2 = g2 * T.p[t] + d;
-          else if (t >= 7) g1 = g1 * T.p[t] + d;
-          else g0 = g0 * T.p[t] + d;
-        }
-        const int64_t a0 = (int64_t)g0 - T.hoff[0], a1 = (int64_t)g1 - T.hoff[1], a2 = (int64_t)g2 - T.hoff[2];
+        const int64_t a0 = (int64_t)horner_group<0, 6>(dp[e], T, P) - T.hoff[0];
+        const int64_t a1 = (ng >= 2) ? (int64_t)horner_group<7, 13>(dp[e], T, P) - T.hoff[1] : 0;
+        const int64_t a2 = (ng == 3) ? (int64_t)horner_group<14, 19>(dp[e], T, P) - T.hoff[2] : 0;
         const int64_t j = j0 + e;
         const int sh = -sa - (j < a.N ? (int)sB[j] + gn.g : 0);
-        if (a.exact) {
-          I128 v = i128_of(ng == 3 ? a2 : (ng == 2 ? a1 : a0));
-          if (ng == 3) v = i128_mul_add(v, (uint64_t)T.m64[1], a1);
-          if (ng >= 2) v = i128_mul_add(v, (uint64_t)T.m64[0], a0);
+        if (EXACT) {
+          I128 v;
+          if (ng == 3) {
+            v = i128_mul_add_s64(a2, (uint64_t)T.m64[1], a1);
+            v = i128_mul_add(v, (uint64_t)T.m64[0], a0);
+          } else if (ng == 2) {
+            v = i128_mul_add_s64(a1, (uint64_t)T.m64[0], a0);
+          } else {
+            v = i128_of(a0);
+          }
           if (CM != 0) v = i128_add_shl(v, cr[e], cshift);
           outv[e] = scale2(i128_to_double(v), sh);
         } else {
@@ -283,11 +321,20 @@ void launch_reconstruct(const ReconArgs& a, const ModTables& T, cudaStream_t s) 
                   (unsigned)std::min<int64_t>((a.MF + 3) / 4, 65535));
   const dim3 block(64, 4);
   if (T.fast_recon) {
-    switch (a.corr_mode) {
-      case 0: reconstruct_fast_kernel<0><<<grid, block, 0, s>>>(a, T); break;
-      case 1: reconstruct_fast_kernel<1><<<grid, block, 0, s>>>(a, T); break;
-      case 2: reconstruct_fast_kernel<2><<<grid, block, 0, s>>>(a, T); break;
-      default: reconstruct_fast_kernel<3><<<grid, block, 0, s>>>(a, T); break;
+    if (a.exact) {
+      switch (a.corr_mode) {
+        case 0: reconstruct_fast_kernel<0, true><<<grid, block, 0, s>>>(a, T); break;
+        case 1: reconstruct_fast_kernel<1, true><<<grid, block, 0, s>>>(a, T); break;
+        case 2: reconstruct_fast_kernel<2, true><<<grid, block, 0, s>>>(a, T); break;
+        default: reconstruct_fast_kernel<3, true><<<grid, block, 0, s>>>(a, T); break;
+      }
+    } else {
+      switch (a.corr_mode) {
+        case 0: reconstruct_fast_kernel<0, false><<<grid, block, 0, s>>>(a, T); break;
+        case 1: reconstruct_fast_kernel<1, false><<<grid, block, 0, s>>>(a, T); break;
+        case 2: reconstruct_fast_kernel<2, false><<<grid, block, 0, s>>>(a, T); break;
+        default: reconstruct_fast_kernel<3, false><<<grid, block, 0, s>>>(a, T); break;
+      }
     }
     return;
   }

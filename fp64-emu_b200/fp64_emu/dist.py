@@ -46,6 +46,17 @@ def rank_block(rank, world, M, N):
     return block_range(M, pr, i), block_range(N, pc, j)
 
 
+def sized_protocol(sizing, maxlg, group=None):
+    """Run this rank's sizing (which fills `maxlg`, the two operand maxima of
+    the log2 norms), then MAX-all-reduce them over the group so every rank
+    derives the single-GPU operand width.  Every rank calls this in the same
+    order; it is the only collective of a partitioned product."""
+    sizing()
+    if dist.is_available() and dist.is_initialized():
+        dist.all_reduce(maxlg, op=dist.ReduceOp.MAX, group=group)
+    return maxlg
+
+
 class ShardedProduct:
     """One rank's share of a partitioned emulated-FP64 product.
 
@@ -71,9 +82,7 @@ class ShardedProduct:
                              self.corr, phases, self.slab_cols)
 
     def sizing(self, out):
-        self._phase(out, PHASE_SIZING)
-        if dist.is_available() and dist.is_initialized():
-            dist.all_reduce(self.maxlg, op=dist.ReduceOp.MAX, group=self.group)
+        sized_protocol(lambda: self._phase(out, PHASE_SIZING), self.maxlg, self.group)
 
     def run(self, out):
         self.sizing(out)

@@ -88,11 +88,21 @@ void orc_col_slabs(int64_t NF, int64_t K, int64_t* kslab, int64_t* nslab) {
 /* Per-column statistics of an operand given as [batch, K, N]
  * (fp64_emu.cu:152-189): each column sums its K slabs sequentially, then the
  * slab partials are combined in slab order. */
+void orc_col_stats_ex(const double* X, int64_t batch, int64_t K, int64_t N, int64_t slab_cols,
+                      int bits, int contract, int16_t* sft, float* lg);
+
 void orc_col_stats(const double* X, int64_t batch, int64_t K, int64_t N, int bits,
                    int contract, int16_t* sft, float* lg) {
+  orc_col_stats_ex(X, batch, K, N, 0, bits, contract, sft, lg);
+}
+
+/* slab_cols > 0 orders the column sums as the slab rule does for that many
+ * columns (a rank holding a slice of the columns reproduces the full run). */
+void orc_col_stats_ex(const double* X, int64_t batch, int64_t K, int64_t N, int64_t slab_cols,
+                      int bits, int contract, int16_t* sft, float* lg) {
   const int64_t NF = batch * N;
   int64_t kslab, nslab;
-  orc_col_slabs(NF, K, &kslab, &nslab);
+  orc_col_slabs(slab_cols > 0 ? slab_cols : NF, K, &kslab, &nslab);
 #pragma omp parallel for schedule(static)
   for (int64_t j = 0; j < NF; j++) {
     const int64_t b = j / N, n = j - b * N;
@@ -374,15 +384,32 @@ void orc_reconstruct(const int8_t* res, const int64_t* corr, int64_t batch, int6
  * Optional outputs (NULL to skip): bits_eff_out, sftA_out [batch*M],
  * sftB_out [batch*N] (shifts after the widening fold).
  * Returns 0, or -1 on bad arguments / allocation failure. */
+int orc_emu_ex(const double* A, const double* B, double* C, int64_t batch, int64_t M, int64_t N,
+               int64_t K, int b_nt, const int32_t* primes, int P, int exact, int bits, int use_corr,
+               int contract, int32_t* bits_eff_out, int16_t* sftA_out, int16_t* sftB_out,
+               int64_t slab_cols, float* maxlg_out, const float* maxlg_in);
+
 int orc_emu(const double* A, const double* B, double* C, int64_t batch, int64_t M, int64_t N,
             int64_t K, int b_nt, const int32_t* primes, int P, int exact, int bits, int use_corr,
             int contract, int32_t* bits_eff_out, int16_t* sftA_out, int16_t* sftB_out) {
+  return orc_emu_ex(A, B, C, batch, M, N, K, b_nt, primes, P, exact, bits, use_corr, contract,
+                    bits_eff_out, sftA_out, sftB_out, 0, NULL, NULL);
+}
+
+/* Extended form for the partitioned protocol: maxlg_out (float[2]) receives
+ * this operand pair's maxima of the log2 norms; maxlg_in, when given, replaces
+ * them in the width rule (the all-reduced maxima); with C == NULL only the
+ * sizing runs. */
+int orc_emu_ex(const double* A, const double* B, double* C, int64_t batch, int64_t M, int64_t N,
+               int64_t K, int b_nt, const int32_t* primes, int P, int exact, int bits, int use_corr,
+               int contract, int32_t* bits_eff_out, int16_t* sftA_out, int16_t* sftB_out,
+               int64_t slab_cols, float* maxlg_out, const float* maxlg_in) {
   if (P < 1 || P > ORC_MAXP || bits < 16 || bits > 53 || batch < 0 || M < 0 || N < 0 || K < 0)
     return -1;
   const int64_t MF = batch * M, NF = batch * N;
   if (MF == 0 || NF == 0) return 0;
   if (K == 0) {
-    memset(C, 0, sizeof(double) * MF * N);
+    if (C) memset(C, 0, sizeof(double) * MF * N);
     return 0;
   }
   int rc = -1;
@@ -394,10 +421,25 @@ int orc_emu(const double* A, const double* B, double* C, int64_t batch, int64_t 
   if (!sA || !sB || !lA || !lB) goto out;
 
   orc_row_stats(A, MF, K, bits, contract, sA, lA);
-  if (b_nt) orc_col_stats(B, batch, K, N, bits, contract, sB, lB);
+  if (b_nt) orc_col_stats_ex(B, batch, K, N, slab_cols, bits, contract, sB, lB);
   else orc_row_stats(B, NF, K, bits, contract, sB, lB);
+  float ma = -INFINITY, mb = -INFINITY;
+  for (int64_t i = 0; i < MF; i++) ma = fmaxf(ma, lA[i]);
+  for (int64_t j = 0; j < NF; j++) mb = fmaxf(mb, lB[j]);
+  if (maxlg_out) {
+    maxlg_out[0] = ma;
+    maxlg_out[1] = mb;
+  }
+  if (!C) {
+    rc = 0;
+    goto out;
+  }
+  if (maxlg_in) {
+    ma = maxlg_in[0];
+    mb = maxlg_in[1];
+  }
   int g = 0;
-  const int be = orc_pick_bits(lA, MF, lB, NF, orc_log2M(primes, P), bits, &g);
+  const int be = orc_pick_bits_from_max(ma, mb, orc_log2M(primes, P), bits, &g);
   for (int64_t i = 0; i < MF; i++) sA[i] = (int16_t)(sA[i] + g);
   for (int64_t j = 0; j < NF; j++) sB[j] = (int16_t)(sB[j] + g);
 

@@ -63,6 +63,9 @@ def lib():
         L.orc_emu.argtypes = [vp, vp, vp, i64, i64, i64, i64, i32, vp, i32, i32, i32, i32, i32,
                               vp, vp, vp]
         L.orc_emu.restype = i32
+        L.orc_emu_ex.argtypes = [vp, vp, vp, i64, i64, i64, i64, i32, vp, i32, i32, i32, i32, i32,
+                                 vp, vp, vp, i64, vp, vp]
+        L.orc_emu_ex.restype = i32
         L.orc_row_stats.argtypes = [vp, i64, i64, i32, i32, vp, vp]
         L.orc_col_stats.argtypes = [vp, i64, i64, i64, i32, i32, vp, vp]
         L.orc_log2M.argtypes = [vp, i32]
@@ -187,3 +190,36 @@ def tables(nprimes):
 
 def cpu_count():
     return len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
+
+
+def emu_shard(A, B, nprimes=None, exact=True, bits=53, corr=None, b_nt=False, slab_cols=0,
+              maxlg_in=None, sizing_only=False):
+    """One rank's share of a partitioned product: returns (C or None, local
+    maxima float32[2]).  maxlg_in replaces the local maxima in the width
+    rule; slab_cols orders the column sums as for that many columns."""
+    A = np.ascontiguousarray(A, dtype=np.float64)
+    B = np.ascontiguousarray(B, dtype=np.float64)
+    A3 = A if A.ndim == 3 else A[None]
+    B3 = B if B.ndim == 3 else B[None]
+    batch, M, K = A3.shape
+    N = B3.shape[2] if b_nt else B3.shape[1]
+    if nprimes is None or corr is None:
+        dp, dc = plan_config(K)
+        nprimes = dp if nprimes is None else nprimes
+        corr = dc if corr is None else corr
+    primes = np.array(PRIMES[:nprimes], dtype=np.int32)
+    C = None if sizing_only else np.empty((batch, M, N), dtype=np.float64)
+    mo = np.zeros(2, dtype=np.float32)
+    mi = None if maxlg_in is None else np.ascontiguousarray(maxlg_in, dtype=np.float32)
+    rc = lib().orc_emu_ex(_p(A3), _p(B3), None if C is None else _p(C), batch, M, N, K,
+                          int(bool(b_nt)), _p(primes), len(primes), int(bool(exact)), int(bits),
+                          int(bool(corr)), int(bool(contract_default)), None, None, None,
+                          int(slab_cols), _p(mo), None if mi is None else _p(mi))
+    if rc != 0:
+        raise RuntimeError("oracle rejected the arguments")
+    if C is not None and A.ndim == 2:
+        C = C[0]
+    return C, mo
+
+
+contract_default = True

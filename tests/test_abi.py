@@ -18,7 +18,7 @@ class Problem(ctypes.Structure):
     _fields_ = [("batch", ctypes.c_int64), ("M", ctypes.c_int64), ("N", ctypes.c_int64),
                 ("K", ctypes.c_int64), ("b_layout", ctypes.c_int32), ("nprimes", ctypes.c_int32),
                 ("primes", ctypes.POINTER(ctypes.c_int32)), ("exact", ctypes.c_int32),
-                ("bits", ctypes.c_int32), ("use_corr", ctypes.c_int32)]
+                ("bits", ctypes.c_int32), ("use_corr", ctypes.c_int32), ("slab_cols", ctypes.c_int64)]
 
 
 PRIMES = [256, 255, 253, 251, 247, 241, 239, 233, 229, 227, 223, 217, 211, 199,
@@ -45,6 +45,15 @@ def declared_symbols():
     return sorted(set(re.findall(r"F64E_API\s+[\w\s\*]+?\b(f64e_\w+)\s*\(", src)))
 
 
+def test_problem_struct_layout_matches_header():
+    # the ctypes mirror above must cover every field of f64e_problem
+    src = open(HEADER).read()
+    body = src[src.index("typedef struct f64e_problem"):src.index("} f64e_problem;")]
+    fields = re.findall(r"^\s+(?:const\s+)?\w+\*?\s+\*?(\w+)(?:,\s*(\w+))?(?:,\s*(\w+))?;", body, re.M)
+    names = [n for grp in fields for n in grp if n]
+    assert names == [f[0] for f in Problem._fields_]
+
+
 def test_header_declares_entry_points():
     names = declared_symbols()
     for n in ("f64e_mm", "f64e_mm_nt", "f64e_bmm", "f64e_bmm_nt", "f64e_mm_timed", "f64e_maxp",
@@ -65,7 +74,7 @@ def _problem(**kw):
     pr = kw.pop("primes", PRIMES[:14])
     arr = (ctypes.c_int32 * len(pr))(*pr)
     p = Problem(batch=1, M=64, N=48, K=512, b_layout=1, nprimes=len(pr), primes=arr, exact=1, bits=53,
-                use_corr=1)
+                use_corr=1, slab_cols=0)
     for k, v in kw.items():
         setattr(p, k, v)
     p._keep = arr

@@ -1,0 +1,124 @@
+"""Multi-rank host logic of the partitioned product, on CPU with gloo ranks.
+
+Each rank takes its block of the 2-D partition (or its batch slice), runs the
+sizing phase (here: the CPU oracle), joins the MAX all-reduce of the two
+operand maxima through fp64_emu.dist.sized_protocol -- the same function the
+GPU path uses -- and computes its block.  The assembled result must be
+bit-identical to the single-process product, which is what makes the
+partitioned GPU runs match a single-GPU run."""
+import os
+import socket
+import sys
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+def _worker(rank, world, port, case, outdir):
+    for p in (ROOT, os.path.join(ROOT, "fp64-emu_b200"), os.path.join(ROOT, "tests")):
+        if p not in sys.path:
+            sys.path.insert(0, p)
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    from datetime import timedelta
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=60))
+    try:
+        from oracle import oracle as O
+        from helpers import make
+        from fp64_emu import dist as proto_mod
+        proto = vars(proto_mod)
+        kind, M, K, N, batch, dname = case
+        if batch == 1:
+            A, Bt = make(dname, M, K, N, seed=3, nt=True)
+            (r0, r1), (c0, c1) = proto["rank_block"](rank, world, M, N)
+            Al, Bl = A[r0:r1], np.ascontiguousarray(Bt[:, c0:c1])
+            slab = N
+        else:
+            pairs = [make(dname, M, K, N, seed=40 + b, nt=True) for b in range(batch)]
+            A = np.stack([p[0] for p in pairs])
+            Bt = np.stack([p[1] for p in pairs])
+            b0, b1 = proto["block_range"](batch, world, rank)
+            Al, Bl = A[b0:b1], Bt[b0:b1]
+            slab = batch * N
+        maxlg = torch.zeros(2, dtype=torch.float32)
+
+        def sizing():
+            _, mo = O.emu_shard(Al, Bl, b_nt=True, slab_cols=slab, sizing_only=True)
+            maxlg.copy_(torch.from_numpy(mo))
+
+        proto["sized_protocol"](sizing, maxlg)
+        C, _ = O.emu_shard(Al, Bl, b_nt=True, slab_cols=slab, maxlg_in=maxlg.numpy())
+        np.save(os.path.join(outdir, f"block{rank}.npy"), C)
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world,case", [
+    (2, ("mm_nt", 64, 300, 48, 1, "wide16")),
+    (4, ("mm_nt", 48, 700, 70, 1, "randn")),
+    (2, ("bmm_nt", 20, 200, 24, 6, "illcond")),
+])
+def test_partitioned_blocks_match_single_process(world, case, tmp_path, oracle_mod):
+    kind, M, K, N, batch, dname = case
+    port = _free_port()
+    mp.start_processes(_worker, args=(world, port, case, str(tmp_path)), nprocs=world, join=True,
+                       start_method="spawn")
+    from helpers import make
+    from fp64_emu import dist as proto_mod
+    proto = vars(proto_mod)
+    if batch == 1:
+        A, Bt = make(dname, M, K, N, seed=3, nt=True)
+        full = oracle_mod.emu(A, Bt, b_nt=True)
+        got = np.empty_like(full)
+        for r in range(world):
+            (r0, r1), (c0, c1) = proto["rank_block"](r, world, M, N)
+            got[r0:r1, c0:c1] = np.load(tmp_path / f"block{r}.npy")
+    else:
+        pairs = [make(dname, M, K, N, seed=40 + b, nt=True) for b in range(batch)]
+        A = np.stack([p[0] for p in pairs])
+        Bt = np.stack([p[1] for p in pairs])
+        full = oracle_mod.emu(A, Bt, b_nt=True)
+        got = np.concatenate([np.load(tmp_path / f"block{r}.npy") for r in range(world)])
+    assert np.array_equal(got.view(np.int64), full.view(np.int64))
+
+
+def test_local_sizing_alone_can_differ():
+    """Without the all-reduce a rank could pick a different operand width: the
+    collective is required, not decorative."""
+    sys.path.insert(0, os.path.join(ROOT, "tests"))
+    from helpers import make
+    from oracle import oracle as O
+    A, Bt = make("spike", 64, 300, 48, seed=3, nt=True)
+    A[32:] = 1.0   # flat rows: larger scaled 2-norms than the spiky half
+    _, m_lo = O.emu_shard(A[:32], Bt, b_nt=True, sizing_only=True)
+    _, m_all = O.emu_shard(A, Bt, b_nt=True, sizing_only=True)
+    assert m_lo[0] < m_all[0]
+    own = O.emu_shard(A[:32], Bt, b_nt=True)[0]
+    shared = O.emu_shard(A[:32], Bt, b_nt=True, maxlg_in=m_all)[0]
+    full = O.emu(A, Bt, b_nt=True)
+    assert np.array_equal(shared, full[:32])
+    assert not np.array_equal(own, full[:32])
+
+
+def test_grid_shapes():
+    from fp64_emu import dist as proto_mod
+    proto = vars(proto_mod)
+    assert [proto["grid_shape"](w) for w in (1, 2, 4, 8)] == [(1, 1), (2, 1), (2, 2), (4, 2)]
+    blocks = [proto["rank_block"](r, 8, 8192, 8192) for r in range(8)]
+    cover = np.zeros((8, 8), dtype=int)
+    for (r0, r1), (c0, c1) in blocks:
+        cover[r0 // 1024:r1 // 1024, c0 // 1024:c1 // 1024] += 1
+    assert (cover == 1).all()

@@ -147,6 +147,11 @@ int get_tables(const int32_t* primes, int P, ModTables* out) {
     const int64_t B = pt * (((1LL << 29) + pt - 1) / pt);
     T.krec[t] = (uint32_t)(kc + B);
   }
+  for (int t = 0; t < P; t++) {
+    uint64_t w = 1;
+    for (int u = (t / 7) * 7; u < t; u++) w *= (uint64_t)primes[u];
+    T.wgrp[t] = w;
+  }
   for (int g = 0; g < 3; g++) {
     int64_t hv = 0;
     for (int t = std::min(g * 7 + 6, P - 1); t >= g * 7; t--) hv = hv * primes[t] + primes[t] / 2;

@@ -75,6 +75,39 @@ __device__ __forceinline__ Split split_elem(double x, int s, int be, bool corr) 
   return S;
 }
 
+// Same split in FP64 for finite x with 2^s a normal double and
+// y = |x| 2^s < 2^53 (every element of a row with a finite maximum): y is
+// exact (products below 2^-1022 round, but such y give T = q = 0 either way);
+// T = RNE(y) from the 2^52 magic add (ulp 1 on [2^52, 2^53), ties to even);
+// q = RNE(256 y) - 256 T = RNE(256 (y - T)) since 256 T is an even integer;
+// hi = RNE(T 2^(7-b)).  Both last roundings use the 1.5 * 2^52 magic, whose
+// low word is the signed result.  Returns false when the conditions fail.
+__device__ __forceinline__ bool split_fast(double x, double p2s, double p2h, int be, bool corr, Split& S) {
+  const uint64_t xb = (uint64_t)__double_as_longlong(x);
+  const double y = __longlong_as_double((long long)(xb & 0x7FFFFFFFFFFFFFFFULL)) * p2s;
+  if (!(y < 9007199254740992.0)) return false;  // y >= 2^53, inf or NaN
+  const bool big = y >= 4503599627370496.0;     // [2^52, 2^53): y is an integer
+  const double z = big ? y : y + 4503599627370496.0;
+  const uint64_t Tu = (uint64_t)__double_as_longlong(z) - (big ? 0x4320000000000000ULL : 0x4330000000000000ULL);
+  const bool neg = (int64_t)xb < 0;
+  S.u = (neg ? (0ULL - Tu) : Tu) + (1ULL << be);
+  if (corr) {
+    const double Td = big ? y : z - 4503599627370496.0;
+    const int r8 = (int)(uint32_t)__double_as_longlong(fma(y - Td, 256.0, 6755399441055744.0));
+    const int h8 = (int)(uint32_t)__double_as_longlong(fma(Td, p2h, 6755399441055744.0));
+    S.h = clamp127(neg ? -h8 : h8);
+    S.q = clamp127(neg ? -r8 : r8);
+  } else {
+    S.h = S.q = 0;
+  }
+  return true;
+}
+
+__device__ __noinline__ Split split_slow(double x, int s, int be, bool corr) { return split_elem(x, s, be, corr); }
+
+// 2^e as a double for -1022 <= e <= 1023.
+__device__ __forceinline__ double pow2d(int e) { return __longlong_as_double((long long)(e + 1023) << 52); }
+
 // Reference form of one residue (fp64_emu.cu:278-287): three 18-bit limbs,
 // 32-bit Barrett with one correction.  Exact whenever u < 2^56; kept for
 // elements beyond that (rows whose maximum is not finite), where the
@@ -152,6 +185,8 @@ __global__ void __launch_bounds__(256) extract_rows_kernel(const ExtractArgs a, 
   const int64_t pstride = a.rows * a.Kp;
   for (int64_t r = (int64_t)blockIdx.y * 8 + threadIdx.y; r < a.rows; r += (int64_t)gridDim.y * 8) {
     const int s = (int)a.sft[r] + gn.g;
+    const bool row_fast = (s >= -960) && (s <= 960);
+    const double p2s = pow2d(row_fast ? s : 0), p2h = pow2d(7 - be);
     const double* __restrict__ xr = a.X + r * a.ld + a.koff;
     for (int64_t ch = (int64_t)blockIdx.x * 32 + threadIdx.x; ch < nch; ch += (int64_t)gridDim.x * 32) {
       const int64_t k0 = ch << 3;
@@ -172,7 +207,7 @@ __global__ void __launch_bounds__(256) extract_rows_kernel(const ExtractArgs a, 
       bool ok = true;
 #pragma unroll
       for (int u = 0; u < 8; u++) {
-        S[u] = split_elem(x[u], s, be, corr);
+        if (!(row_fast && split_fast(x[u], p2s, p2h, be, corr, S[u]))) S[u] = split_slow(x[u], s, be, corr);
         ok = ok && (S[u].u >> 56) == 0;
       }
       // The reference form only for chunks holding an element of a row with a
@@ -223,6 +258,8 @@ __global__ void __launch_bounds__(256) extract_cols_kernel(const ExtractArgs a, 
   const int64_t n = n0 + tx;
   const bool nin = n < a.N;
   const int s = nin ? (int)a.sft[b * a.N + n] + gn.g : 0;
+  const bool col_fast = (s >= -960) && (s <= 960);
+  const double p2s = pow2d(col_fast ? s : 0), p2h = pow2d(7 - be);
   const double* __restrict__ xb = a.X + b * a.K * a.N + n;
 #pragma unroll
   for (int qi = 0; qi < 2; qi++) {
@@ -234,7 +271,7 @@ __global__ void __launch_bounds__(256) extract_cols_kernel(const ExtractArgs a, 
     for (int u = 0; u < 4; u++) {
       const int64_t k = kb + u;
       const double x = (nin && k < a.K) ? __ldg(xb + k * a.N) : 0.0;
-      S[u] = split_elem(x, s, be, corr);
+      if (!(col_fast && split_fast(x, p2s, p2h, be, corr, S[u]))) S[u] = split_slow(x, s, be, corr);
       ok = ok && (S[u].u >> 56) == 0;
     }
     if (ok) {

@@ -43,6 +43,7 @@ struct ModTables {
   uint32_t krec[kMaxP];
   uint32_t mrec[kMaxP];        // ceil(2^39 / p)
   int64_t hoff[3];             // Horner value of the offsets h per 7-modulus group
+  uint64_t wgrp[kMaxP];        // radix weight of digit t inside its 7-modulus group
   int fast_recon;              // every modulus > 128
 };
 

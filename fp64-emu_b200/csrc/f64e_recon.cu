@@ -67,26 +67,6 @@ __device__ __forceinline__ I128 i128_mul_add_s64(int64_t a, uint64_t m, int64_t 
   return r;
 }
 
-// Horner value of the offset digits t = lo .. hi of one group (hi - lo <= 6):
-// the first three steps stay below 2^32, the rest run in 64 bits.
-template <int LO, int HI>
-__device__ __forceinline__ uint64_t horner_group(const uint32_t (&dp)[kGroups], const ModTables& T, int P) {
-  uint32_t g32 = 0;
-  uint64_t g64 = 0;
-  int steps = 0;
-#pragma unroll
-  for (int t = HI; t >= LO; t--) {
-    if (t >= P) continue;
-    const uint32_t d = __byte_perm(dp[t >> 2], 0u, 0x4440u | (uint32_t)(t & 3));
-    if (steps == 0) g32 = d;
-    else if (steps < 4) g32 = g32 * T.p[t] + d;
-    else if (steps == 4) g64 = (uint64_t)g32 * T.p[t] + d;
-    else g64 = g64 * T.p[t] + d;
-    steps++;
-  }
-  return steps <= 4 ? (uint64_t)g32 : g64;
-}
-
 // a + c * 2^s for 0 < s < 64.
 __device__ __forceinline__ I128 i128_add_shl(I128 a, int64_t c, int s) {
   const uint64_t clo = (uint64_t)c << s;
@@ -242,7 +222,7 @@ __global__ void __launch_bounds__(256, 2) reconstruct_fast_kernel(const ReconArg
   const bool vec_out = ((a.N & 3) == 0) && ((reinterpret_cast<uintptr_t>(a.C) & 15) == 0);
   for (int64_t i = (int64_t)blockIdx.y * 4 + threadIdx.y; i < a.MF; i += (int64_t)gridDim.y * 4) {
     const int sa = (int)a.sftA[i] + gn.g;
-    const int16_t* __restrict__ sB = a.sftB + (i / a.M) * a.N;
+    const int16_t* __restrict__ sB = a.sftB + (a.M == a.MF ? 0 : (i / a.M) * a.N);
     for (int64_t jq = (int64_t)blockIdx.x * 64 + threadIdx.x; jq < nq; jq += (int64_t)gridDim.x * 64) {
       const int64_t j0 = jq << 2;
       const int64_t off = i * a.ldn + j0;
@@ -253,10 +233,21 @@ __global__ void __launch_bounds__(256, 2) reconstruct_fast_kernel(const ReconArg
       int64_t cr[4];
       load_corr<CM>(a, off, plane, cr);
       uint32_t dp[4][kGroups];
+      // Group values as digit-weighted sums, accumulated as the digits come:
+      // the first four digits of a group (weights < 2^24) in 32 bits, the
+      // rest in 64; unused digit positions hold 0 and add nothing.
+      uint32_t glo[4][3];
+      uint64_t ghi[4][3];
 #pragma unroll
-      for (int e = 0; e < 4; e++)
+      for (int e = 0; e < 4; e++) {
 #pragma unroll
         for (int g = 0; g < kGroups; g++) dp[e][g] = 0;
+#pragma unroll
+        for (int g = 0; g < 3; g++) {
+          glo[e][g] = 0;
+          ghi[e][g] = 0;
+        }
+      }
 #pragma unroll
       for (int t = 0; t < kMaxP; t++) {
         if (t >= P) break;
@@ -271,14 +262,16 @@ __global__ void __launch_bounds__(256, 2) reconstruct_fast_kernel(const ReconArg
           const uint32_t X = (uint32_t)((rt - (int)acc) * mi) + kr;   // in [0, 2^31)
           const uint32_t d = X - (__umulhi(X, mr) >> 7) * p;          // d + h in [0, p)
           dp[e][t >> 2] = __byte_perm(dp[e][t >> 2], d, insert_sel(t & 3));
+          if (t % 7 < 4) glo[e][t / 7] += d * (uint32_t)T.wgrp[t];
+          else ghi[e][t / 7] += (uint64_t)d * T.wgrp[t];
         }
       }
       double outv[4];
 #pragma unroll
       for (int e = 0; e < 4; e++) {
-        const int64_t a0 = (int64_t)horner_group<0, 6>(dp[e], T, P) - T.hoff[0];
-        const int64_t a1 = (ng >= 2) ? (int64_t)horner_group<7, 13>(dp[e], T, P) - T.hoff[1] : 0;
-        const int64_t a2 = (ng == 3) ? (int64_t)horner_group<14, 19>(dp[e], T, P) - T.hoff[2] : 0;
+        const int64_t a0 = (int64_t)(ghi[e][0] + glo[e][0]) - T.hoff[0];
+        const int64_t a1 = (ng >= 2) ? (int64_t)(ghi[e][1] + glo[e][1]) - T.hoff[1] : 0;
+        const int64_t a2 = (ng == 3) ? (int64_t)(ghi[e][2] + glo[e][2]) - T.hoff[2] : 0;
         const int64_t j = j0 + e;
         const int sh = -sa - (j < a.N ? (int)sB[j] + gn.g : 0);
         if (EXACT) {

@@ -462,6 +462,20 @@ int check_batch(int64_t batch, int32_t nprimes, int32_t use_corr) {
 
 }  // namespace
 
+namespace f64e {
+
+// Internal entry for other translation units of the library (the
+// allocation-free entry point): the generic product on a given workspace.
+int run_problem(const f64e_problem* p, const double* A, const double* B, double* out, void* ws, size_t ws_bytes,
+                void* stream, int phases) {
+  g_err.clear();
+  return run(p, A, B, out, ws, ws_bytes, stream, phases, false, nullptr);
+}
+
+int report_error(int code, const char* msg) { return fail(code, "%s", msg); }
+
+}  // namespace f64e
+
 extern "C" {
 
 int64_t f64e_maxp(void) { return kMaxP; }

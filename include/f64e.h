@@ -159,6 +159,27 @@ F64E_API int f64e_gemm_checked(const f64e_problem* p, const double* A, const dou
 F64E_API int f64e_debug_fetch(const f64e_problem* p, const void* workspace, int which, void* host, size_t cap,
                      size_t* nbytes, void* stream);
 
+/* Size of the device scratch array behind f64e_mm_nt_noalloc: 64 MiB, enough
+ * for products up to roughly M = N = K = 1100 at the default plan. */
+#define F64E_NOALLOC_SCRATCH_BYTES (64ull << 20)
+
+/* f64e_mm_nt for callers that cannot allocate device memory (code inside
+ * another framework's memory arena, plugin hosts and real-time paths that may
+ * not call cudaMalloc / cudaFree, sandboxed deployments without an allocator).
+ * No counterpart in the reference.  Same arguments and result as f64e_mm_nt,
+ * minus the workspace: the product runs in a file-scope device array of
+ * F64E_NOALLOC_SCRATCH_BYTES, held on every GPU where this entry point has
+ * been used until the process exits.  Problems needing more scratch are
+ * rejected with F64E_ERR_WORKSPACE.  Nothing is allocated.  All calls on a
+ * device share the one array (it keeps the last call's contents; nothing in
+ * it needs to start at zero): calls whose work overlaps on the GPU race and
+ * must be serialized by the caller.  The first call on each device looks up
+ * the array's device address (cudaGetSymbolAddress) and should come before
+ * any stream capture. */
+F64E_API int f64e_mm_nt_noalloc(double* out, const double* A, const double* Bt, int64_t M, int64_t N, int64_t K,
+                                const int32_t* primes, int32_t nprimes, int32_t exact, int64_t bits,
+                                int32_t use_corr, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

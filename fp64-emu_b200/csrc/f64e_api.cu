@@ -19,6 +19,7 @@
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <map>
 #include <mutex>
@@ -54,6 +55,13 @@ int fail(int code, const char* fmt, ...) {
   va_end(ap);
   g_err = buf;
   return code;
+}
+
+// F64E_GEMM_SINGLE=1 keeps every product on the one-CTA GEMM (A/B checks of
+// the CTA-pair kernel); read per call.
+bool gemm_force_single() {
+  const char* v = std::getenv("F64E_GEMM_SINGLE");
+  return v && v[0] == '1';
 }
 
 int cuda_fail(cudaError_t e, const char* what) {
@@ -343,10 +351,14 @@ int run_gemm(const Plan& l, const ModTables& T, void* ws, const Dev& d, bool che
     launch_residue_gemm_check(at<int8_t>(ws, l.o_pA), at<int8_t>(ws, l.o_pB), l.MF, l.NF, g, T, s);
   } else {
     CUtensorMap tA, tB;
-    if (!encode_plane_map(&tA, at<int8_t>(ws, l.o_pA), (int64_t)l.G * l.batch, l.M, l.Kp, gemm_block_rows_a()) ||
-        !encode_plane_map(&tB, at<int8_t>(ws, l.o_pB), (int64_t)l.G * l.batch, l.N, l.Kp, gemm_block_rows_b()))
+    const bool pair = gemm_use_pair(g.M) && !gemm_force_single();
+    const int rows_a = pair ? gemm_pair_block_rows() : gemm_block_rows_a();
+    const int rows_b = pair ? gemm_pair_block_rows() : gemm_block_rows_b();
+    if (!encode_plane_map(&tA, at<int8_t>(ws, l.o_pA), (int64_t)l.G * l.batch, l.M, l.Kp, rows_a) ||
+        !encode_plane_map(&tB, at<int8_t>(ws, l.o_pB), (int64_t)l.G * l.batch, l.N, l.Kp, rows_b))
       return fail(F64E_ERR_CUDA, "cuTensorMapEncodeTiled rejected the plane layout");
-    const cudaError_t e = launch_residue_gemm(tA, tB, g, T, d.sms, s);
+    const cudaError_t e = pair ? launch_residue_gemm_pair(tA, tB, g, T, d.sms, s)
+                               : launch_residue_gemm(tA, tB, g, T, d.sms, s);
     if (e != cudaSuccess) return cuda_fail(e, "modular GEMM launch");
   }
   const cudaError_t e = cudaGetLastError();

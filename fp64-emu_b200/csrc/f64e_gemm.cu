@@ -45,16 +45,18 @@ struct Tile {
   int64_t out;  // element offset of the output slot
 };
 
+template <int TBM = BM, int TGM = GROUP_M>
 __device__ __forceinline__ Tile decode_tile(int tile, const GemmArgs& g) {
-  const int ntm = (g.M + BM - 1) / BM, ntn = (g.N + BN - 1) / BN;
+  constexpr int GROUP_M_ = TGM;
+  const int ntm = (g.M + TBM - 1) / TBM, ntn = (g.N + BN - 1) / BN;
   const int tps = ntm * ntn;
   const int ncs = g.corr_mode == 1 ? g.batch : (g.corr_mode == 2 ? 2 * g.batch : 0);
   const int slot = tile / tps, r = tile - slot * tps;
-  const int gsz = GROUP_M * ntn;
+  const int gsz = GROUP_M_ * ntn;
   const int gi = r / gsz, o = r - gi * gsz;
-  const int mf = gi * GROUP_M, mh = min(GROUP_M, ntm - mf);
+  const int mf = gi * GROUP_M_, mh = min(GROUP_M_, ntm - mf);
   Tile T;
-  T.m0 = (mf + o % mh) * BM;
+  T.m0 = (mf + o % mh) * TBM;
   T.n0 = (o / mh) * BN;
   const int64_t slot_elems = (int64_t)g.M * g.ldn;
   if (slot < ncs) {
@@ -83,8 +85,9 @@ __device__ __forceinline__ Tile decode_tile(int tile, const GemmArgs& g) {
   return T;
 }
 
-__device__ __forceinline__ int total_tiles(const GemmArgs& g) {
-  const int ntm = (g.M + BM - 1) / BM, ntn = (g.N + BN - 1) / BN;
+template <int TBM = BM>
+__device__ __host__ __forceinline__ int total_tiles(const GemmArgs& g) {
+  const int ntm = (g.M + TBM - 1) / TBM, ntn = (g.N + BN - 1) / BN;
   const int ncs = g.corr_mode == 1 ? g.batch : (g.corr_mode == 2 ? 2 * g.batch : 0);
   return ntm * ntn * (g.P * g.batch + ncs);
 }
@@ -264,6 +267,207 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   }
 }
 
+// ---------------------------------------------------------------------------
+// CTA-pair form (cta_group::2): a cluster of two CTAs on two SMs computes a
+// 256 x 256 tile.  CTA r loads A rows [m0 + 128 r, +128) and B rows
+// [n0 + 128 r, +128) into its own shared memory (no multicast); both loads
+// complete on the leader's (rank 0) full barrier; the leader's MMA thread
+// issues M=256, N=256, K=32 tcgen05.mma over both CTAs' tiles and commits
+// stage releases and finished accumulators to both CTAs at once.  Each
+// CTA's epilogue drains its own 128 TMEM lanes and signals the leader.
+// Per SM this halves the B-operand traffic through shared memory, which at
+// the INT8 MMA rate is what limits the one-CTA 128 x 256 tile.
+namespace {
+constexpr int PBM = 256, PHALF = 128, PSTAGES = 6, PGROUP_M = 8;
+constexpr uint32_t PA_BYTES = PHALF * BK, PB_BYTES = PHALF * BK, PSTAGE_BYTES = PA_BYTES + PB_BYTES;
+constexpr size_t PSMEM_BYTES = 1024 + (size_t)PSTAGES * PSTAGE_BYTES + 256;
+constexpr uint32_t PIDESC = idesc_i8(PBM, BN);
+}  // namespace
+
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    residue_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmapA, const __grid_constant__ CUtensorMap tmapB,
+                             const GemmArgs g, const ModTables T) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_s = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + (((raw_s + 1023u) & ~1023u) - raw_s);
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + PSTAGES * PA_BYTES;
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + PSTAGES * PSTAGE_BYTES);
+  uint64_t* empty_bar = full_bar + PSTAGES;
+  uint64_t* acc_full = empty_bar + PSTAGES;
+  uint64_t* acc_empty = acc_full + 2;
+  uint64_t* drain_bar = acc_empty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int cluster = blockIdx.x >> 1, nclusters = gridDim.x >> 1;
+  const int ntiles = total_tiles<PBM>(g);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < PSTAGES; s++) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    for (int a = 0; a < 2; a++) {
+      mbar_init(&acc_full[a], 1);
+      mbar_init(&acc_empty[a], 2 * 4);  // one elected lane per epilogue warp of both CTAs
+    }
+    mbar_init(drain_bar, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+    tma_prefetch_desc(&tmapA);
+    tma_prefetch_desc(&tmapB);
+  }
+  __syncwarp();
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  __syncwarp();
+  cluster_sync();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const uint64_t lim = g.wait_limit_ns;
+  const uint32_t full0 = mapa_shared(smem_u32(&full_bar[0]), 0);     // leader's full barriers
+  const uint32_t accempty0 = mapa_shared(smem_u32(&acc_empty[0]), 0);  // leader's accumulator-empty
+
+  if (warp == 0) {
+    // ---------------------------------------------------------- producer --
+    if (elect_one()) {
+      uint32_t j = 0;
+      bool ok = true;
+      for (int tile = cluster; tile < ntiles && ok; tile += nclusters) {
+        const Tile tl = decode_tile<PBM, PGROUP_M>(tile, g);
+        for (int kb = 0; kb < tl.nk; kb++, j++) {
+          const uint32_t s = j % PSTAGES, ph = (j / PSTAGES) & 1;
+          if (!mbar_wait(&empty_bar[s], ph ^ 1, lim, g.status, kWaitEmpty) || *abort_flag) {
+            *abort_flag = 1;
+            ok = false;
+            break;
+          }
+          const bool second = kb >= g.nkb;
+          const int z = second ? tl.z1 : tl.z0;
+          const int kx = (second ? kb - g.nkb : kb) * BK;
+          if (leader) mbar_arrive_expect_tx(&full_bar[s], 2 * PSTAGE_BYTES);
+          tma_load_3d_pair(sA + s * PA_BYTES, &tmapA, kx, tl.m0 + PHALF * (int)rank, z, full0 + 8 * s);
+          tma_load_3d_pair(sB + s * PB_BYTES, &tmapB, kx, tl.n0 + PHALF * (int)rank, z, full0 + 8 * s);
+        }
+      }
+      // Drain: the leader's full barriers count both CTAs' bytes, so once they
+      // complete every copy of the pair has landed.
+      if (leader) {
+        const uint32_t first = j > (uint32_t)PSTAGES ? j - PSTAGES : 0;
+        for (uint32_t jj = first; jj < j; jj++)
+          mbar_wait(&full_bar[jj % PSTAGES], (jj / PSTAGES) & 1, lim, g.status, kWaitDrain);
+      }
+    }
+  } else if (warp == 1) {
+    // --------------------------------------------------------- MMA issuer --
+    if (leader && elect_one()) {
+      uint32_t j = 0, it = 0;
+      bool ok = true;
+      for (int tile = cluster; tile < ntiles && ok; tile += nclusters, it++) {
+        const Tile tl = decode_tile<PBM, PGROUP_M>(tile, g);
+        const uint32_t a = it & 1, aph = (it >> 1) & 1;
+        if (!mbar_wait(&acc_empty[a], aph ^ 1, lim, g.status, kWaitAccEmpty) || *abort_flag) {
+          *abort_flag = 1;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + a * BN;
+        for (int kb = 0; kb < tl.nk; kb++, j++) {
+          const uint32_t s = j % PSTAGES, ph = (j / PSTAGES) & 1;
+          if (!mbar_wait(&full_bar[s], ph, lim, g.status, kWaitFull) || *abort_flag) {
+            *abort_flag = 1;
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(sA + s * PA_BYTES), b_addr = smem_u32(sB + s * PB_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < BK / 32; kk++)
+            mma_i8_pair(d_tmem, smem_desc_sw128(a_addr + kk * 32), smem_desc_sw128(b_addr + kk * 32), PIDESC,
+                        (kb | kk) != 0);
+          tc_commit_pair(&empty_bar[s], 0x3);
+        }
+        if (ok) tc_commit_pair(&acc_full[a], 0x3);
+      }
+      tc_commit_pair(drain_bar, 0x1);
+      mbar_wait(drain_bar, 0, lim, g.status, kWaitDrain);
+    }
+  } else {
+    // ----------------------------------------------------------- epilogue --
+    const int q = warp & 3;
+    const int row_l = q * 32 + lane;
+    uint32_t it = 0;
+    for (int tile = cluster; tile < ntiles; tile += nclusters, it++) {
+      const Tile tl = decode_tile<PBM, PGROUP_M>(tile, g);
+      const uint32_t a = it & 1, aph = (it >> 1) & 1;
+      if (!mbar_wait(&acc_full[a], aph, lim, g.status, kWaitAccFull) || *abort_flag) {
+        *abort_flag = 1;
+        break;
+      }
+      tc_fence_after();
+      const int row = tl.m0 + PHALF * (int)rank + row_l;
+      const bool row_ok = row < g.M;
+      const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + a * BN;
+      if (tl.kind == 0) {
+        const uint32_t p = T.p[tl.t], md = T.mdiv[tl.t], off = T.off[tl.t];
+        int8_t* orow = g.res + tl.out + (int64_t)row * g.ldn;
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; c++) {
+          uint32_t v[32];
+          tmem_ld_32x32b_x32(taddr + c * 32, v);
+          tmem_wait_ld();
+          uint32_t w[8];
+#pragma unroll
+          for (int i = 0; i < 8; i++) {
+            uint32_t x = 0;
+#pragma unroll
+            for (int e = 0; e < 4; e++)
+              x |= (uint32_t)(uint8_t)(int8_t)bal_mod_s32((int)v[4 * i + e], p, md, off) << (8 * e);
+            w[i] = x;
+          }
+          const int col = tl.n0 + c * 32;
+          if (row_ok && col < g.ldn)
+            *reinterpret_cast<uint4*>(orow + col) = make_uint4(w[0], w[1], w[2], w[3]);
+          if (row_ok && col + 16 < g.ldn)
+            *reinterpret_cast<uint4*>(orow + col + 16) = make_uint4(w[4], w[5], w[6], w[7]);
+        }
+      } else {
+        int32_t* orow = g.corr + tl.out + (int64_t)row * g.ldn;
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; c++) {
+          uint32_t v[32];
+          tmem_ld_32x32b_x32(taddr + c * 32, v);
+          tmem_wait_ld();
+          const int col = tl.n0 + c * 32;
+#pragma unroll
+          for (int i = 0; i < 8; i++)
+            if (row_ok && col + 4 * i < g.ldn)
+              *reinterpret_cast<uint4*>(orow + col + 4 * i) = make_uint4(v[4 * i], v[4 * i + 1], v[4 * i + 2],
+                                                                         v[4 * i + 3]);
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(accempty0 + 8 * a);
+    }
+  }
+
+  tc_fence_before();
+  __syncwarp();
+  cluster_sync();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, TMEM_COLS);
+  }
+}
+
 // 3-D tensor map over K-major planes [zdim][rows][Kp] (uint8), box
 // (128 bytes of K) x box_rows x 1, 128-byte swizzle, zero fill outside.
 bool encode_plane_map(CUtensorMap* map, const void* base, int64_t zdim, int64_t rows, int64_t Kp, int box_rows) {
@@ -290,6 +494,8 @@ bool encode_plane_map(CUtensorMap* map, const void* base, int64_t zdim, int64_t 
 
 int gemm_block_rows_a() { return BM; }
 int gemm_block_rows_b() { return BN; }
+int gemm_pair_block_rows() { return PHALF; }
+bool gemm_use_pair(int M) { return M > BM; }
 
 cudaError_t launch_residue_gemm(const CUtensorMap& tA, const CUtensorMap& tB, const GemmArgs& g, const ModTables& T,
                                 int num_sms, cudaStream_t s) {
@@ -307,6 +513,47 @@ cudaError_t launch_residue_gemm(const CUtensorMap& tA, const CUtensorMap& tB, co
   const int grid = (int)std::min<int64_t>(tiles, num_sms);
   residue_gemm_tc_kernel<<<grid, NUM_THREADS, SMEM_BYTES, s>>>(tA, tB, g, T);
   return cudaGetLastError();
+}
+
+cudaError_t launch_residue_gemm_pair(const CUtensorMap& tA, const CUtensorMap& tB, const GemmArgs& g,
+                                     const ModTables& T, int num_sms, cudaStream_t s) {
+  const int64_t tiles = total_tiles<PBM>(g);
+  if (tiles <= 0) return cudaSuccess;
+  static int max_clusters = -1;
+  if (max_clusters < 0) {
+    cudaError_t e =
+        cudaFuncSetAttribute(residue_gemm_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)PSMEM_BYTES);
+    if (e != cudaSuccess) return e;
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.gridDim = dim3(2 * (num_sms / 2), 1, 1);
+    cfg.blockDim = dim3(NUM_THREADS, 1, 1);
+    cfg.dynamicSmemBytes = PSMEM_BYTES;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    e = cudaOccupancyMaxActiveClusters(&n, residue_gemm_pair_kernel, &cfg);
+    if (e != cudaSuccess) return e;
+    max_clusters = std::max(n, 1);
+  }
+  const int clusters = (int)std::min<int64_t>(tiles, max_clusters);
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.gridDim = dim3(2 * clusters, 1, 1);
+  cfg.blockDim = dim3(NUM_THREADS, 1, 1);
+  cfg.dynamicSmemBytes = PSMEM_BYTES;
+  cfg.stream = s;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, residue_gemm_pair_kernel, tA, tB, g, T);
 }
 
 }  // namespace f64e

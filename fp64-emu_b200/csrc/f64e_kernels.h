@@ -56,8 +56,12 @@ struct GemmArgs {
 bool encode_plane_map(CUtensorMap* map, const void* base, int64_t zdim, int64_t rows, int64_t Kp, int box_rows);
 int gemm_block_rows_a();
 int gemm_block_rows_b();
+int gemm_pair_block_rows();   // box rows of both operands in the CTA-pair kernel
+bool gemm_use_pair(int M);    // CTA-pair kernel for tall problems
 cudaError_t launch_residue_gemm(const CUtensorMap& tA, const CUtensorMap& tB, const GemmArgs& g, const ModTables& T,
                                 int num_sms, cudaStream_t s);
+cudaError_t launch_residue_gemm_pair(const CUtensorMap& tA, const CUtensorMap& tB, const GemmArgs& g,
+                                     const ModTables& T, int num_sms, cudaStream_t s);
 
 // ---- reference-form modular GEMM for validation (f64e_gemm_check.cu) ----
 // Plain dp4a kernel with the same inputs and outputs as the tcgen05 kernel;

@@ -41,7 +41,7 @@ import torch.distributed as dist  # noqa: E402
 
 METRIC = "emulated FP64 TFLOP/s (2MNK/t) at n=8192"
 UNIT = "TFLOP/s"
-PROFILE_SUMMARY = os.path.join(ROOT, "profiles", "residue_gemm_tc_mm_nt_8192.md")
+PROFILE_SUMMARY = os.path.join(ROOT, "profiles", "residue_gemm_pair_mm_nt_8192.md")
 
 WORKLOADS = {
     # name: (kind, batch, M, N, K, dist, nprimes, corr)
@@ -532,7 +532,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="C2", choices=sorted(WORKLOADS))
     ap.add_argument("--seed", type=int, default=0)
-    ap.add_argument("--cpu-rows", type=int, default=128)
+    ap.add_argument("--cpu-rows", type=int, default=512)
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baselines")
     ap.add_argument("--no-native", action="store_true", help="skip the cuBLAS DGEMM context number")
     args = ap.parse_args()

@@ -167,9 +167,14 @@ def profiled_traffic_per_launch():
 
 # ----------------------------------------------------------- our product --
 class Step:
-    """One rank's product, phase by phase on the current stream, with a
-    preallocated workspace (the public entry points allocate the same
-    workspace from torch's caching allocator per call)."""
+    """One rank's product on the current stream with a preallocated workspace
+    (the public entry points allocate the same workspace from torch's caching
+    allocator per call): sizing (+ the MAX all-reduce when partitioned), then
+    extraction, GEMM and reconstruction in one call, which the library runs as
+    a chunked pipeline for large products.  With events, every GEMM launch of
+    the step is bracketed by two of them on the stream it runs on."""
+
+    MAX_LAUNCHES = 16
 
     def __init__(self, kind, A, B, nprimes, corr, slab_cols):
         import fp64_emu
@@ -183,16 +188,25 @@ class Step:
         self.nprimes, self.corr = self.sp.primes.numel(), self.sp.corr
         self.fp64_emu = fp64_emu
 
-    def run(self, ev_g0=None, ev_g1=None):
+    def new_events(self):
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(2 * self.MAX_LAUNCHES)]
+        for e in ev:
+            e.record()   # creates the underlying CUDA event
+        return ev
+
+    def run(self, events=None):
+        """Returns the number of GEMM launches of the step."""
         sp, out = self.sp, self.out
         sp.sizing(out)
-        sp._phase(out, 2)
-        if ev_g0 is not None:
-            ev_g0.record()
-        sp._phase(out, 4)
-        if ev_g1 is not None:
-            ev_g1.record()
-        sp._phase(out, 8)
+        if events is None:
+            sp._phase(out, 14)
+            return 0
+        return self.fp64_emu.ops.fp64_emu_gemm_ws_ev(out, sp.ws, sp.A, sp.B, sp.primes, sp.b_kn, sp.exact, sp.bits,
+                                                     sp.corr, 14, sp.slab_cols, [e.cuda_event for e in events])
+
+    @staticmethod
+    def gemm_ms(events, launches):
+        return sum(events[2 * i].elapsed_time(events[2 * i + 1]) for i in range(launches))
 
 
 def barrier():
@@ -208,11 +222,13 @@ def max_over_ranks(x):
     return float(t.item())
 
 
-def our_kernel_launches_per_step(kind, batch, K):
+def our_kernel_launches_per_step(kind, batch, chunks):
     # sizing: row stats of A + (column partial + finalize, or row stats) of B
-    # + operand maxima; extraction of A and B; one GEMM; one reconstruction.
+    # + operand maxima; per chunk one extraction of A, one GEMM and one
+    # reconstruction; B extracted once (single product) or per chunk (batch).
     nt = kind in ("mm_nt", "bmm_nt")
-    return (1 + (2 if nt else 1) + 1) + 2 + 1 + 1
+    c = max(1, chunks)
+    return (1 + (2 if nt else 1) + 1) + 3 * c + (1 if batch == 1 else c)
 
 
 def cpu_baseline_oracle(A_cpu, Bt_cpu, nprimes, corr, rows):
@@ -299,7 +315,9 @@ def run_ours(args):
         step.run()
     torch.cuda.synchronize()
 
-    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    ev = [step.new_events() for _ in range(args.steps)]
+    launches = [0] * args.steps
+    torch.cuda.synchronize()
     clocks = ClockSampler(dev)
     clocks.start()
     barrier()
@@ -308,12 +326,12 @@ def run_ours(args):
     t_stop = torch.cuda.Event(enable_timing=True)
     t_start.record()
     for i in range(args.steps):
-        step.run(ev[i][0], ev[i][1])
+        launches[i] = step.run(ev[i])
     t_stop.record()
     torch.cuda.synchronize()
     barrier()
     ms_local = t_start.elapsed_time(t_stop) / args.steps
-    gemm_ms_local = sum(a.elapsed_time(b) for a, b in ev) / args.steps
+    gemm_ms_local = sum(Step.gemm_ms(ev[i], launches[i]) for i in range(args.steps)) / args.steps
 
     # e2e through the public API with host buffers.
     import fp64_emu
@@ -392,7 +410,8 @@ def run_ours(args):
                    "compute": "s8 x s8 -> s32 tcgen05 residue GEMMs, exact int128 recombine"},
         "e2e": {"value": round(work / (e2e_ms * 1e-3) / 1e12, 3), "unit": UNIT, "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "api": "fp64_emu." + kind if world == 1 else "fp64_emu.dist"},
-        "gpu_launches": our_kernel_launches_per_step(kind, batch, K) * args.steps,
+        "gpu_launches": sum(our_kernel_launches_per_step(kind, A_l.shape[0] if A_l.dim() == 3 else 1, c)
+                            for c in launches),
         "roofline": {"bound": "tensor", "kernel": "residue_gemm_pair_kernel" if Ml > 128 else "residue_gemm_tc_kernel",
                      "achieved": round(achieved, 1), "peak": round(peak, 1), "unit": "TOPS (int8)",
                      "frac": round(achieved / peak, 4),
@@ -401,7 +420,8 @@ def run_ours(args):
                                   f"nominal 8192 MAC/clk/SM at the sampled clock = {nominal:.0f} TOPS, "
                                   f"frac of nominal {achieved / nominal:.3f}",
                      "gemm_ms_per_step": round(gemm_ms, 4), "traffic": traffic},
-        "phases_ms": {"gemm": round(gemm_ms, 4), "other": round(ms - gemm_ms, 4)},
+        "phases_ms": {"gemm_busy": round(gemm_ms, 4), "outside_gemm": round(ms - gemm_ms, 4),
+                      "gemm_launches_per_step": launches[-1] if launches else 0},
         "clocks": clk,
     }
     if world > 1:

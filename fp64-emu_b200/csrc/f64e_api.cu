@@ -248,6 +248,7 @@ int make_plan(const f64e_problem* p, Plan* L) {
 }
 
 struct Dev {
+  int dev = 0;
   int sms = 0;
   bool ok = false;
 };
@@ -262,6 +263,7 @@ int device_info(Dev* d) {
   auto it = cache.find(dev);
   if (it == cache.end()) {
     Dev v;
+    v.dev = dev;
     int major = 0, minor = 0;
     e = cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
     if (e == cudaSuccess) e = cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
@@ -296,96 +298,307 @@ int run_sizing(const Plan& l, const double* A, const double* B, void* ws, cudaSt
   return F64E_OK;
 }
 
-// Extraction of one K window [k0, k0 + kw) of both operands.
-void run_extract(const Plan& l, const ModTables& T, const double* A, const double* B, void* ws, int64_t k0,
-                 int64_t kw, cudaStream_t s) {
-  WsHead* head = at<WsHead>(ws, 0);
+// A view of the product: the whole problem, or one chunk of it (a block of
+// rows of A and C for a single product, a block of members for a batch).  Each
+// chunk owns a contiguous share of every intermediate buffer in the chunk's
+// own layout ([G][members][rows][Kp] planes, [P][members * rows][ldn]
+// residues), so the kernels see it as a product of its own.
+struct View {
+  int64_t batch, M;            // members and rows of A / C in this view
+  const double* A;             // [batch][M][K]
+  const double* B;             // [batch][N][K] or [batch][K][N]
+  const int16_t* sftA;         // [batch * M]
+  const int16_t* sftB;         // [batch * N]
+  int8_t* pA;                  // [G][batch][M][Kp]
+  int8_t* pB;                  // [G][batch][N][Kp]
+  int8_t* res;                 // [P][batch * M][ldn]
+  int32_t* corr;               // [ncorr][batch * M][ldn]
+  double* C;                   // [batch * M][N]
+};
+
+int ncorr_planes(const Plan& l) { return l.gemm_corr == 2 ? 2 : (l.gemm_corr == 1 ? 1 : 0); }
+
+View full_view(const Plan& l, const double* A, const double* B, void* ws, double* out) {
+  View v;
+  v.batch = l.batch;
+  v.M = l.M;
+  v.A = A;
+  v.B = B;
+  v.sftA = at<int16_t>(ws, l.o_sftA);
+  v.sftB = at<int16_t>(ws, l.o_sftB);
+  v.pA = at<int8_t>(ws, l.o_pA);
+  v.pB = at<int8_t>(ws, l.o_pB);
+  v.res = at<int8_t>(ws, l.o_res);
+  v.corr = at<int32_t>(ws, l.o_corr);
+  v.C = out;
+  return v;
+}
+
+// Rows [r0, r1) of a single product (B shared by every chunk).
+View row_chunk(const Plan& l, const View& f, int64_t r0, int64_t r1) {
+  View v = f;
+  v.M = r1 - r0;
+  v.A = f.A + r0 * l.K;
+  v.sftA = f.sftA + r0;
+  v.pA = f.pA + (int64_t)l.G * r0 * l.Kp;
+  v.res = f.res + (int64_t)l.P * r0 * l.ldn;
+  v.corr = f.corr + (int64_t)ncorr_planes(l) * r0 * l.ldn;
+  v.C = f.C + r0 * l.N;
+  return v;
+}
+
+// Members [b0, b1) of a batch (both operands per chunk).
+View batch_chunk(const Plan& l, const View& f, int64_t b0, int64_t b1) {
+  View v = f;
+  v.batch = b1 - b0;
+  v.A = f.A + b0 * l.M * l.K;
+  v.B = f.B + b0 * l.N * l.K;
+  v.sftA = f.sftA + b0 * l.M;
+  v.sftB = f.sftB + b0 * l.N;
+  v.pA = f.pA + (int64_t)l.G * b0 * l.M * l.Kp;
+  v.pB = f.pB + (int64_t)l.G * b0 * l.N * l.Kp;
+  v.res = f.res + (int64_t)l.P * b0 * l.M * l.ldn;
+  v.corr = f.corr + (int64_t)ncorr_planes(l) * b0 * l.M * l.ldn;
+  v.C = f.C + b0 * l.M * l.N;
+  return v;
+}
+
+ExtractArgs extract_args(const Plan& l, void* ws, int64_t k0, int64_t kw) {
   ExtractArgs ea{};
-  ea.X = A;
-  ea.rows = l.MF;
   ea.K = kw;
   ea.Kp = l.Kp;
   ea.ld = l.K;
   ea.koff = k0;
-  ea.batch = l.batch;
   ea.N = l.N;
-  ea.sft = at<int16_t>(ws, l.o_sftA);
-  ea.maxlg = head->maxlg;
+  ea.maxlg = at<WsHead>(ws, 0)->maxlg;
   ea.bits = l.bits;
   ea.use_corr = l.use_corr;
-  ea.hi_plane = l.P;      // A planes: [residues, hi, q]
+  return ea;
+}
+
+// Extraction of one K window [k0, k0 + kw) of A (planes [residues, hi, q]).
+void extract_A(const Plan& l, const ModTables& T, const View& v, void* ws, int64_t k0, int64_t kw, cudaStream_t s) {
+  ExtractArgs ea = extract_args(l, ws, k0, kw);
+  ea.X = v.A;
+  ea.rows = v.batch * v.M;
+  ea.batch = v.batch;
+  ea.sft = v.sftA;
+  ea.hi_plane = l.P;
   ea.q_plane = l.P + 1;
-  ea.planes = at<int8_t>(ws, l.o_pA);
+  ea.planes = v.pA;
   launch_extract_rows(ea, T, s);
-  ExtractArgs eb = ea;
-  eb.X = B;
-  eb.rows = l.NF;
-  eb.sft = at<int16_t>(ws, l.o_sftB);
-  eb.q_plane = l.P;       // B planes: [residues, q, hi]
+}
+
+// Extraction of one K window of B (planes [residues, q, hi]).
+void extract_B(const Plan& l, const ModTables& T, const View& v, void* ws, int64_t k0, int64_t kw, cudaStream_t s) {
+  ExtractArgs eb = extract_args(l, ws, k0, kw);
+  eb.X = v.B;
+  eb.rows = v.batch * l.N;
+  eb.batch = v.batch;
+  eb.sft = v.sftB;
+  eb.q_plane = l.P;
   eb.hi_plane = l.P + 1;
-  eb.planes = at<int8_t>(ws, l.o_pB);
+  eb.planes = v.pB;
   if (l.nt) launch_extract_cols(eb, T, s);
   else launch_extract_rows(eb, T, s);
 }
 
-GemmArgs gemm_args(const Plan& l, void* ws) {
+GemmArgs gemm_args(const Plan& l, const View& v, void* ws) {
   GemmArgs g{};
-  g.M = (int)l.M;
+  g.M = (int)v.M;
   g.N = (int)l.N;
-  g.batch = (int)l.batch;
+  g.batch = (int)v.batch;
   g.P = l.P;
   g.Kp = (int)l.Kp;
   g.nkb = (int)((l.Kp + 127) / 128);
   g.corr_mode = l.gemm_corr;
   g.ldn = (int)l.ldn;
-  g.res = at<int8_t>(ws, l.o_res);
-  g.corr = at<int32_t>(ws, l.o_corr);
+  g.res = v.res;
+  g.corr = v.corr;
   g.status = &at<WsHead>(ws, 0)->status;
   g.wait_limit_ns = g_wait_limit.load();
   return g;
 }
 
-int run_gemm(const Plan& l, const ModTables& T, void* ws, const Dev& d, bool checked, cudaStream_t s) {
-  const GemmArgs g = gemm_args(l, ws);
-  if (checked) {
-    launch_residue_gemm_check(at<int8_t>(ws, l.o_pA), at<int8_t>(ws, l.o_pB), l.MF, l.NF, g, T, s);
-  } else {
-    CUtensorMap tA, tB;
-    const bool pair = gemm_use_pair(g.M) && !gemm_force_single();
-    const int rows_a = pair ? gemm_pair_block_rows() : gemm_block_rows_a();
-    const int rows_b = pair ? gemm_pair_block_rows() : gemm_block_rows_b();
-    if (!encode_plane_map(&tA, at<int8_t>(ws, l.o_pA), (int64_t)l.G * l.batch, l.M, l.Kp, rows_a) ||
-        !encode_plane_map(&tB, at<int8_t>(ws, l.o_pB), (int64_t)l.G * l.batch, l.N, l.Kp, rows_b))
-      return fail(F64E_ERR_CUDA, "cuTensorMapEncodeTiled rejected the plane layout");
-    const cudaError_t e = pair ? launch_residue_gemm_pair(tA, tB, g, T, d.sms, s)
-                               : launch_residue_gemm(tA, tB, g, T, d.sms, s);
-    if (e != cudaSuccess) return cuda_fail(e, "modular GEMM launch");
-  }
-  const cudaError_t e = cudaGetLastError();
+// Tensor maps of one view's planes for the kernel gemm_use_pair picks.
+int gemm_maps(const Plan& l, const View& v, CUtensorMap* tA, CUtensorMap* tB) {
+  const bool pair = gemm_use_pair((int)v.M) && !gemm_force_single();
+  const int rows_a = pair ? gemm_pair_block_rows() : gemm_block_rows_a();
+  const int rows_b = pair ? gemm_pair_block_rows() : gemm_block_rows_b();
+  if (!encode_plane_map(tA, v.pA, (int64_t)l.G * v.batch, v.M, l.Kp, rows_a) ||
+      !encode_plane_map(tB, v.pB, (int64_t)l.G * v.batch, l.N, l.Kp, rows_b))
+    return fail(F64E_ERR_CUDA, "cuTensorMapEncodeTiled rejected the plane layout");
+  return F64E_OK;
+}
+
+int launch_gemm_view(const Plan& l, const ModTables& T, const View& v, const CUtensorMap& tA, const CUtensorMap& tB,
+                     void* ws, const Dev& d, cudaStream_t s) {
+  const GemmArgs g = gemm_args(l, v, ws);
+  const bool pair = gemm_use_pair(g.M) && !gemm_force_single();
+  cudaError_t e = pair ? launch_residue_gemm_pair(tA, tB, g, T, d.sms, s) : launch_residue_gemm(tA, tB, g, T, d.sms, s);
+  if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "modular GEMM launch");
   return F64E_OK;
 }
 
-void run_reconstruct(const Plan& l, const ModTables& T, void* ws, double* out, cudaStream_t s) {
+int run_gemm(const Plan& l, const ModTables& T, const View& v, void* ws, const Dev& d, bool checked, cudaStream_t s) {
+  if (checked) {
+    const GemmArgs g = gemm_args(l, v, ws);
+    launch_residue_gemm_check(v.pA, v.pB, v.batch * v.M, v.batch * l.N, g, T, s);
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e, "modular GEMM launch");
+    return F64E_OK;
+  }
+  CUtensorMap tA, tB;
+  const int rc = gemm_maps(l, v, &tA, &tB);
+  if (rc) return rc;
+  return launch_gemm_view(l, T, v, tA, tB, ws, d, s);
+}
+
+void run_reconstruct(const Plan& l, const ModTables& T, const View& v, void* ws, int corr_mode, const void* corr,
+                     cudaStream_t s) {
   ReconArgs r{};
-  r.res = at<int8_t>(ws, l.o_res);
-  r.corr_mode = l.recon_corr;
-  r.corr = l.recon_corr == 3 ? (const void*)at<int64_t>(ws, l.o_cacc) : (const void*)at<int32_t>(ws, l.o_corr);
-  r.MF = l.MF;
-  r.M = l.M;
+  r.res = v.res;
+  r.corr_mode = corr_mode;
+  r.corr = corr;
+  r.MF = v.batch * v.M;
+  r.M = v.M;
   r.N = l.N;
   r.ldn = l.ldn;
-  r.sftA = at<int16_t>(ws, l.o_sftA);
-  r.sftB = at<int16_t>(ws, l.o_sftB);
+  r.sftA = v.sftA;
+  r.sftB = v.sftB;
   r.maxlg = at<WsHead>(ws, 0)->maxlg;
   r.bits = l.bits;
   r.exact = l.exact;
-  r.C = out;
+  r.C = v.C;
   launch_reconstruct(r, T, s);
 }
 
+// ------------------------------------------------------------ pipelining --
+// A product whose three compute phases run in one call is cut into chunks
+// (rows of A and C, or members of a batch).  The GEMM of chunk c runs on a
+// high-priority library stream while the extraction of later chunks (a
+// low-priority library stream) and the reconstruction of earlier ones (the
+// caller's stream) share the SMs with it: the persistent GEMM holds one CTA
+// per SM and leaves registers for one block of either kernel.  Results are
+// the same bits as the unchunked product: every element's arithmetic is
+// independent of the chunking and the sizing covers the whole product.
+constexpr int kPipeMaxChunks = 16;
+constexpr int kPipeEvents = 2 * kPipeMaxChunks + 2;
+
+struct PipeRes {
+  cudaStream_t hi = nullptr, aux = nullptr;
+  cudaEvent_t ev[kPipeEvents] = {};
+  std::mutex mtx;
+};
+
+// Per-device streams and events, created on first use and kept for the
+// process.  Returns nullptr (and the product runs unchunked) while the
+// caller's stream is being captured and they do not exist yet.
+PipeRes* pipe_res(int dev, cudaStream_t s, int* rc) {
+  static std::mutex mtx;
+  static std::map<int, PipeRes*> all;
+  *rc = F64E_OK;
+  std::lock_guard<std::mutex> lk(mtx);
+  auto it = all.find(dev);
+  if (it != all.end()) return it->second;
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(s, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone) return nullptr;
+  int lo = 0, hi = 0;
+  cudaError_t e = cudaDeviceGetStreamPriorityRange(&lo, &hi);
+  PipeRes* r = new PipeRes;
+  if (e == cudaSuccess) e = cudaStreamCreateWithPriority(&r->hi, cudaStreamNonBlocking, hi);
+  if (e == cudaSuccess) e = cudaStreamCreateWithPriority(&r->aux, cudaStreamNonBlocking, lo);
+  for (int i = 0; i < kPipeEvents && e == cudaSuccess; i++) e = cudaEventCreateWithFlags(&r->ev[i], cudaEventDisableTiming);
+  if (e != cudaSuccess) {
+    *rc = cuda_fail(e, "pipeline streams");
+    return nullptr;
+  }
+  all.emplace(dev, r);
+  return r;
+}
+
+// F64E_PIPE_CHUNK=<n> sets the chunk extent (rows of a single product,
+// members of a batch) and F64E_PIPE_CHUNK=0 turns chunking off; read per
+// call (A/B checks of the chunked path against the unchunked one).
+int64_t pipe_chunk_override() {
+  const char* v = std::getenv("F64E_PIPE_CHUNK");
+  if (!v || !*v) return -1;
+  return std::max<int64_t>(0, std::atoll(v));
+}
+
+// Chunk extent for a product, 0 when it runs unchunked.
+int64_t pipe_chunk(const Plan& l, bool* by_batch) {
+  *by_batch = l.batch > 1;
+  const int64_t extent = *by_batch ? l.batch : l.M;
+  int64_t per = 0;
+  const int64_t ov = pipe_chunk_override();
+  if (ov >= 0) {
+    per = ov;
+  } else if (*by_batch) {
+    // members of 2048 or more rows in all, eight chunks at most
+    if (l.MF >= 2048 && l.batch >= 4) per = (l.batch + 7) / 8;
+  } else if (l.M >= 2048) {
+    const int64_t n = std::min<int64_t>(8, l.M / 1024);
+    per = round_up((l.M + n - 1) / n, 256);
+  }
+  if (per <= 0 || per >= extent) return 0;
+  if ((extent + per - 1) / per > kPipeMaxChunks) per = (extent + kPipeMaxChunks - 1) / kPipeMaxChunks;
+  return per;
+}
+
+int run_pipelined(const Plan& l, const ModTables& T, const View& f, void* ws, const Dev& d, PipeRes* pr,
+                  int64_t per, bool by_batch, cudaStream_t s, void* const* gev, int ngev, int* launches) {
+  const int64_t extent = by_batch ? l.batch : l.M;
+  const int C = (int)((extent + per - 1) / per);
+  std::vector<View> v(C);
+  std::vector<CUtensorMap> tA(C), tB(C);
+  for (int c = 0; c < C; c++) {
+    const int64_t a0 = c * per, a1 = std::min(extent, a0 + per);
+    v[c] = by_batch ? batch_chunk(l, f, a0, a1) : row_chunk(l, f, a0, a1);
+    const int rc = gemm_maps(l, v[c], &tA[c], &tB[c]);   // all host-side failures before the first launch
+    if (rc) return rc;
+  }
+  std::lock_guard<std::mutex> lk(pr->mtx);
+  cudaEvent_t* E = pr->ev;   // E[0] fork, E[c] chunk c extracted, E[C + c] chunk c multiplied, E[2C] aux done
+  if (!by_batch) extract_B(l, T, f, ws, 0, l.K, s);
+  extract_A(l, T, v[0], ws, 0, l.K, s);
+  if (by_batch) extract_B(l, T, v[0], ws, 0, l.K, s);
+  cudaError_t e = cudaEventRecord(E[0], s);
+  if (e == cudaSuccess) e = cudaStreamWaitEvent(pr->hi, E[0], 0);
+  if (e == cudaSuccess) e = cudaStreamWaitEvent(pr->aux, E[0], 0);
+  if (e != cudaSuccess) return cuda_fail(e, "pipeline fork");
+  for (int c = 1; c < C; c++) {
+    extract_A(l, T, v[c], ws, 0, l.K, pr->aux);
+    if (by_batch) extract_B(l, T, v[c], ws, 0, l.K, pr->aux);
+    cudaEventRecord(E[c], pr->aux);
+  }
+  cudaEventRecord(E[2 * C], pr->aux);
+  int rc = F64E_OK;
+  for (int c = 0; c < C; c++) {
+    if (c > 0) cudaStreamWaitEvent(pr->hi, E[c], 0);
+    if (2 * c + 1 < ngev) cudaEventRecord(static_cast<cudaEvent_t>(gev[2 * c]), pr->hi);
+    if (rc == F64E_OK) rc = launch_gemm_view(l, T, v[c], tA[c], tB[c], ws, d, pr->hi);
+    if (2 * c + 1 < ngev) cudaEventRecord(static_cast<cudaEvent_t>(gev[2 * c + 1]), pr->hi);
+    cudaEventRecord(E[C + c], pr->hi);
+  }
+  const int cm = l.recon_corr;
+  for (int c = 0; c < C; c++) {
+    cudaStreamWaitEvent(s, E[C + c], 0);
+    run_reconstruct(l, T, v[c], ws, cm, v[c].corr, s);
+  }
+  e = cudaStreamWaitEvent(s, E[2 * C], 0);   // join the extraction stream
+  if (launches) *launches = C;
+  if (rc) return rc;
+  if (e == cudaSuccess) e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "pipelined launch");
+  return F64E_OK;
+}
+
 int run(const f64e_problem* p, const double* A, const double* B, double* out, void* ws, size_t ws_bytes,
-        void* stream, int phases, bool checked, cudaEvent_t* ev) {
+        void* stream, int phases, bool checked, cudaEvent_t* ev, void* const* gev = nullptr, int ngev = 0,
+        int* launches = nullptr) {
+  if (launches) *launches = 0;
   Plan l;
   int rc = make_plan(p, &l);
   if (rc) return rc;
@@ -415,25 +628,45 @@ int run(const f64e_problem* p, const double* A, const double* B, double* out, vo
     if (rc) return rc;
   }
   if (!(phases & F64E_PHASE_COMPUTE)) return F64E_OK;
+  const View f = full_view(l, A, B, ws, out);
+  if (!ev && !checked && !l.deep && (phases & F64E_PHASE_COMPUTE) == F64E_PHASE_COMPUTE) {
+    bool by_batch = false;
+    const int64_t per = pipe_chunk(l, &by_batch);
+    if (per > 0) {
+      PipeRes* pr = pipe_res(d.dev, s, &rc);
+      if (rc) return rc;
+      if (pr) return run_pipelined(l, T, f, ws, d, pr, per, by_batch, s, gev, ngev, launches);
+    }
+  }
   if (!l.deep) {
-    if (phases & F64E_PHASE_EXTRACT) run_extract(l, T, A, B, ws, 0, l.K, s);
+    if (phases & F64E_PHASE_EXTRACT) {
+      extract_A(l, T, f, ws, 0, l.K, s);
+      extract_B(l, T, f, ws, 0, l.K, s);
+    }
     if (ev) cudaEventRecord(ev[1], s);
     if (phases & F64E_PHASE_GEMM) {
-      rc = run_gemm(l, T, ws, d, checked, s);
+      if (ngev >= 2) cudaEventRecord(static_cast<cudaEvent_t>(gev[0]), s);
+      rc = run_gemm(l, T, f, ws, d, checked, s);
       if (rc) return rc;
+      if (ngev >= 2) cudaEventRecord(static_cast<cudaEvent_t>(gev[1]), s);
+      if (launches) *launches = 1;
     }
   } else if (phases & (F64E_PHASE_EXTRACT | F64E_PHASE_GEMM)) {
     if ((phases & (F64E_PHASE_EXTRACT | F64E_PHASE_GEMM)) != (F64E_PHASE_EXTRACT | F64E_PHASE_GEMM))
       return fail(F64E_ERR_ARGUMENT, "deep-K products run EXTRACT and GEMM together");
     const int64_t nres = (int64_t)l.P * l.MF * l.ldn, ncorr = l.use_corr ? l.MF * l.ldn : 0;
     for (int sgi = 0; sgi < l.nseg; sgi++) {
-      const int64_t k0 = (int64_t)sgi * l.Kseg;
-      run_extract(l, T, A, B, ws, k0, std::min(l.Kseg, l.K - k0), s);
-      rc = run_gemm(l, T, ws, d, checked, s);
+      const int64_t k0 = (int64_t)sgi * l.Kseg, kw = std::min(l.Kseg, l.K - k0);
+      extract_A(l, T, f, ws, k0, kw, s);
+      extract_B(l, T, f, ws, k0, kw, s);
+      if (2 * sgi + 1 < ngev) cudaEventRecord(static_cast<cudaEvent_t>(gev[2 * sgi]), s);
+      rc = run_gemm(l, T, f, ws, d, checked, s);
       if (rc) return rc;
+      if (2 * sgi + 1 < ngev) cudaEventRecord(static_cast<cudaEvent_t>(gev[2 * sgi + 1]), s);
       launch_deepk_accum(at<int8_t>(ws, l.o_res), at<int32_t>(ws, l.o_racc), nres, at<int32_t>(ws, l.o_corr),
                          at<int64_t>(ws, l.o_cacc), ncorr, sgi == 0, s);
     }
+    if (launches) *launches = l.nseg;
     launch_deepk_fold(at<int32_t>(ws, l.o_racc), at<int8_t>(ws, l.o_res), l.MF * l.ldn, T, s);
     if (ev) cudaEventRecord(ev[1], s);
   }
@@ -441,7 +674,10 @@ int run(const f64e_problem* p, const double* A, const double* B, double* out, vo
     cudaEventRecord(ev[2], s);
     cudaEventRecord(ev[3], s);
   }
-  if (phases & F64E_PHASE_RECON) run_reconstruct(l, T, ws, out, s);
+  if (phases & F64E_PHASE_RECON) {
+    const void* corr = l.recon_corr == 3 ? (const void*)at<int64_t>(ws, l.o_cacc) : (const void*)f.corr;
+    run_reconstruct(l, T, f, ws, l.recon_corr, corr, s);
+  }
   if (ev) cudaEventRecord(ev[4], s);
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "kernel launch");
@@ -502,6 +738,16 @@ int f64e_gemm(const f64e_problem* p, const double* A, const double* B, double* o
               void* stream, int phases) {
   g_err.clear();
   return run(p, A, B, out, ws, ws_bytes, stream, phases, false, nullptr);
+}
+
+int f64e_gemm_ev(const f64e_problem* p, const double* A, const double* B, double* out, void* ws, size_t ws_bytes,
+                 void* stream, int phases, void* const* events, int32_t n_events, int32_t* launches) {
+  g_err.clear();
+  if (n_events > 0 && !events) return fail(F64E_ERR_ARGUMENT, "null event array");
+  int nl = 0;
+  const int rc = run(p, A, B, out, ws, ws_bytes, stream, phases, false, nullptr, events, std::max(0, n_events), &nl);
+  if (launches) *launches = nl;
+  return rc;
 }
 
 int f64e_gemm_checked(const f64e_problem* p, const double* A, const double* B, double* out, void* ws,

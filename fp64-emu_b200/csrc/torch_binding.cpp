@@ -200,7 +200,8 @@ int64_t workspace_bytes(const at::Tensor& A, const at::Tensor& B, const at::Tens
 
 void gemm_phase(at::Tensor& out, at::Tensor& ws, const at::Tensor& A, const at::Tensor& B,
                 const at::Tensor& primes_cpu, bool b_kn, bool exact, int64_t bits, bool use_corr, int64_t phases,
-                bool checked, int64_t slab_cols) {
+                bool checked, int64_t slab_cols, const std::vector<int64_t>* events = nullptr,
+                int32_t* launches = nullptr) {
   TORCH_CHECK(A.is_cuda() && B.is_cuda() && A.dtype() == at::kDouble && B.dtype() == at::kDouble,
               "A,B must be f64 CUDA");
   TORCH_CHECK(A.is_contiguous() && B.is_contiguous() && out.is_contiguous() && ws.is_contiguous(), "contig");
@@ -214,15 +215,34 @@ void gemm_phase(at::Tensor& out, at::Tensor& ws, const at::Tensor& A, const at::
   if (checked)
     check(f64e_gemm_checked(&p, A.data_ptr<double>(), B.data_ptr<double>(), out.data_ptr<double>(), ws.data_ptr(),
                             nb, stream_of()));
-  else
+  else if (events) {
+    std::vector<void*> ev(events->size());
+    for (size_t i = 0; i < ev.size(); i++) ev[i] = reinterpret_cast<void*>((*events)[i]);
+    check(f64e_gemm_ev(&p, A.data_ptr<double>(), B.data_ptr<double>(), out.data_ptr<double>(), ws.data_ptr(), nb,
+                       stream_of(), (int)phases, ev.data(), (int32_t)ev.size(), launches));
+  } else {
     check(f64e_gemm(&p, A.data_ptr<double>(), B.data_ptr<double>(), out.data_ptr<double>(), ws.data_ptr(), nb,
                     stream_of(), (int)phases));
+  }
 }
 
 void gemm_ws(at::Tensor& out, at::Tensor& ws, const at::Tensor& A, const at::Tensor& B,
              const at::Tensor& primes_cpu, bool b_kn, bool exact, int64_t bits, bool use_corr, int64_t phases,
              int64_t slab_cols) {
   gemm_phase(out, ws, A, B, primes_cpu, b_kn, exact, bits, use_corr, phases, false, slab_cols);
+}
+
+// gemm_ws that brackets each modular-GEMM launch with two of the given CUDA
+// events (raw cudaEvent_t handles, e.g. torch.cuda.Event.cuda_event) and
+// returns the number of GEMM launches.
+int64_t gemm_ws_ev(at::Tensor& out, at::Tensor& ws, const at::Tensor& A, const at::Tensor& B,
+                   const at::Tensor& primes_cpu, bool b_kn, bool exact, int64_t bits, bool use_corr, int64_t phases,
+                   int64_t slab_cols, at::IntArrayRef events) {
+  for (const int64_t e : events) TORCH_CHECK(e != 0, "events must be created (record them once first)");
+  const std::vector<int64_t> ev(events.begin(), events.end());
+  int32_t launches = 0;
+  gemm_phase(out, ws, A, B, primes_cpu, b_kn, exact, bits, use_corr, phases, false, slab_cols, &ev, &launches);
+  return launches;
 }
 
 void gemm_checked(at::Tensor& out, at::Tensor& ws, const at::Tensor& A, const at::Tensor& B,
@@ -278,6 +298,9 @@ TORCH_LIBRARY(fp64_emu_b200, ops) {
       "fp64_emu_gemm_ws(Tensor! out, Tensor! ws, Tensor A, Tensor B, Tensor primes_cpu, bool b_kn, bool exact, "
       "int bits, bool use_corr, int phases, int slab_cols=0) -> ()");
   ops.def(
+      "fp64_emu_gemm_ws_ev(Tensor! out, Tensor! ws, Tensor A, Tensor B, Tensor primes_cpu, bool b_kn, bool exact, "
+      "int bits, bool use_corr, int phases, int slab_cols, int[] events) -> int");
+  ops.def(
       "fp64_emu_gemm_checked(Tensor! out, Tensor! ws, Tensor A, Tensor B, Tensor primes_cpu, bool b_kn, bool "
       "exact, int bits, bool use_corr) -> ()");
   ops.def("fp64_emu_status(Tensor ws) -> int");
@@ -297,6 +320,7 @@ TORCH_LIBRARY_IMPL(fp64_emu_b200, CUDA, ops) {
   ops.impl("fp64_emu_bmm_nt", &bmm_nt);
   ops.impl("fp64_emu_mm_timed", &mm_timed);
   ops.impl("fp64_emu_gemm_ws", &gemm_ws);
+  ops.impl("fp64_emu_gemm_ws_ev", &gemm_ws_ev);
   ops.impl("fp64_emu_gemm_checked", &gemm_checked);
   ops.impl("fp64_emu_status", &status);
   ops.impl("fp64_emu_debug_fetch", &debug_fetch);

@@ -63,7 +63,15 @@ enum {
  * A partitioned multi-GPU caller MAX-all-reduces the two floats between
  * SIZING and the rest, so every rank uses the single-GPU operand width.
  * Deep-K problems (K > 131071) interleave EXTRACT and GEMM per segment and
- * need both bits in the same call. */
+ * need both bits in the same call.
+ * A call that runs EXTRACT, GEMM and RECON together may cut the product into
+ * chunks (rows of A and C, or batch members) and overlap the chunks' phases
+ * on two library-owned streams forked from and joined back to the caller's
+ * stream; the result is the same bits.  The intermediate planes it leaves in
+ * the workspace are then in the chunks' own layout, so a later call that runs
+ * GEMM or RECON alone needs the preceding phases run as separate calls.  The
+ * first such call on a device creates those streams; a call made while the
+ * caller's stream is being captured before that runs unchunked. */
 enum {
   F64E_PHASE_SIZING = 1,
   F64E_PHASE_EXTRACT = 2,
@@ -101,6 +109,15 @@ F64E_API size_t f64e_workspace_size(const f64e_problem* p);
  * workspace. */
 F64E_API int f64e_gemm(const f64e_problem* p, const double* A, const double* B, double* out, void* workspace,
               size_t workspace_bytes, void* stream, int phases);
+
+/* f64e_gemm that also brackets every modular-GEMM launch with two caller
+ * events (cudaEvent_t, created with timing): launch i records events[2i]
+ * before and events[2i + 1] after it, on the stream the launch runs on, for
+ * i < n_events / 2.  *launches receives the number of GEMM launches (chunks,
+ * or K segments).  Measurement aid with no reference counterpart. */
+F64E_API int f64e_gemm_ev(const f64e_problem* p, const double* A, const double* B, double* out, void* workspace,
+                 size_t workspace_bytes, void* stream, int phases, void* const* events, int32_t n_events,
+                 int32_t* launches);
 
 /* out[M,N] = A[M,K] @ B[N,K]^T.  Replaces fp64_emu_mm (fp64_emu.cu:1583-1608):
  * K <= 8,388,608 (deep K runs K-segmented), bits in [16, 53]. */

@@ -1,0 +1,149 @@
+"""Chunked products: a call that runs extraction, GEMM and reconstruction
+together cuts the product into chunks (rows of A and C, or batch members) and
+overlaps the chunks' phases on library streams.  Every chunked product must be
+bit-identical to the same product run unchunked (F64E_PIPE_CHUNK=0) and to the
+CPU oracle.  F64E_PIPE_CHUNK=<n> forces the chunk extent, so ragged and
+many-chunk cases run at sizes the oracle finishes in seconds."""
+import os
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+
+from helpers import make, same_bits  # noqa: E402
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def emu():
+    if not torch.cuda.is_available():
+        pytest.skip("CUDA required")
+    import fp64_emu
+    return fp64_emu
+
+
+class chunk:
+    """Set F64E_PIPE_CHUNK for the duration of a block."""
+
+    def __init__(self, n):
+        self.n = n
+
+    def __enter__(self):
+        self.old = os.environ.get("F64E_PIPE_CHUNK")
+        if self.n is None:
+            os.environ.pop("F64E_PIPE_CHUNK", None)
+        else:
+            os.environ["F64E_PIPE_CHUNK"] = str(self.n)
+
+    def __exit__(self, *a):
+        if self.old is None:
+            os.environ.pop("F64E_PIPE_CHUNK", None)
+        else:
+            os.environ["F64E_PIPE_CHUNK"] = self.old
+
+
+def _pair(kind, batch, M, K, N, dist, seed):
+    nt = kind.endswith("_nt")
+    if batch == 1:
+        A, B = make(dist, M, K, N, seed=seed, nt=nt)
+    else:
+        pairs = [make(dist, M, K, N, seed=seed + b, nt=nt) for b in range(batch)]
+        A, B = np.stack([p[0] for p in pairs]), np.stack([p[1] for p in pairs])
+    return A, B
+
+
+CASES = [
+    # (kind, batch, M, K, N, dist, chunk, kwargs)
+    ("mm_nt", 1, 1000, 700, 300, "randn", 384, {}),          # 3 chunks, the last ragged
+    ("mm_nt", 1, 777, 513, 259, "wide16", 128, {}),          # 7 chunks of single-CTA GEMMs
+    ("mm", 1, 1030, 900, 520, "illcond40", 512, {}),
+    ("mm", 1, 600, 1000, 200, "spike", 256, {"nprimes": 13, "corr": False}),
+    ("mm_nt", 1, 640, 600, 333, "randn", 256, {"exact": False}),
+    ("mm_nt", 1, 520, 300, 90, "wide8", 200, {"bits": 40}),
+    ("mm", 1, 300, 200, 100, "randn", 100, {"nprimes": 20}),
+    ("bmm_nt", 10, 60, 200, 150, "illcond", 3, {}),          # member chunks 3, 3, 3, 1
+    ("bmm", 7, 90, 333, 77, "randn", 2, {}),
+    ("mm_nt", 1, 512, 70000, 64, "randn", 256, {}),          # K > 65536: two correction planes
+]
+
+
+@pytest.mark.parametrize("case", CASES, ids=lambda c: f"{c[0]}-{c[1]}x{c[2]}x{c[3]}x{c[4]}-{c[5]}-c{c[6]}")
+def test_chunked_matches_unchunked_and_oracle(emu, oracle_mod, case):
+    kind, batch, M, K, N, dist, per, kw = case
+    A, B = _pair(kind, batch, M, K, N, dist, seed=M + K + N)
+    fn = getattr(emu, kind)
+    Ad, Bd = torch.from_numpy(A).cuda(), torch.from_numpy(B).cuda()
+    with chunk(0):
+        flat = fn(Ad, Bd, **kw)
+    with chunk(per):
+        chunked = fn(Ad, Bd, **kw)
+    torch.cuda.synchronize()
+    assert torch.equal(chunked, flat)
+    W = oracle_mod.emu(A, B, b_nt=kind.endswith("_nt"), **kw)
+    assert same_bits(chunked.cpu().numpy(), W)
+
+
+@pytest.mark.parametrize("kind,shape", [("mm_nt", (4096, 2048, 1024)), ("mm", (2304, 1024, 2048)),
+                                        ("bmm_nt", (8, 256, 512, 384))])
+def test_default_chunking_matches_unchunked(emu, kind, shape):
+    # sizes where the default policy chunks (M >= 2048, or >= 4 members of >= 2048 rows in all)
+    g = torch.Generator(device="cuda").manual_seed(sum(shape))
+    if kind == "bmm_nt":
+        b, M, K, N = shape
+        A = torch.randn(b, M, K, dtype=torch.float64, device="cuda", generator=g)
+        B = torch.randn(b, K, N, dtype=torch.float64, device="cuda", generator=g)
+    else:
+        M, K, N = shape
+        A = torch.randn(M, K, dtype=torch.float64, device="cuda", generator=g)
+        B = torch.randn((K, N) if kind == "mm_nt" else (N, K), dtype=torch.float64, device="cuda", generator=g)
+    fn = getattr(emu, kind)
+    with chunk(None):
+        auto = fn(A, B)
+    with chunk(0):
+        flat = fn(A, B)
+    torch.cuda.synchronize()
+    assert torch.equal(auto, flat)
+
+
+def test_gemm_events_count_chunk_launches(emu):
+    A = torch.randn(1000, 640, dtype=torch.float64, device="cuda")
+    Bt = torch.randn(640, 300, dtype=torch.float64, device="cuda")
+    pr = emu._tables(14)[0]
+    ws = torch.empty(emu.ops.fp64_emu_workspace_bytes(A, Bt, pr, True, True), dtype=torch.uint8, device="cuda")
+    out = torch.empty(1000, 300, dtype=torch.float64, device="cuda")
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(8)]
+    for e in ev:
+        e.record()
+    with chunk(256):
+        emu.ops.fp64_emu_gemm_ws(out, ws, A, Bt, pr, True, True, 53, True, 1, 0)
+        n = emu.ops.fp64_emu_gemm_ws_ev(out, ws, A, Bt, pr, True, True, 53, True, 14, 0, [e.cuda_event for e in ev])
+    torch.cuda.synchronize()
+    assert n == 4
+    assert all(ev[2 * i].elapsed_time(ev[2 * i + 1]) > 0 for i in range(4))
+    with chunk(0):
+        assert torch.equal(out, emu.mm_nt(A, Bt))
+    assert emu.ops.fp64_emu_status(ws) == 0
+
+
+def test_chunked_product_in_a_cuda_graph(emu):
+    A = torch.randn(1100, 500, dtype=torch.float64, device="cuda")
+    Bt = torch.randn(500, 260, dtype=torch.float64, device="cuda")
+    with chunk(300):
+        for _ in range(2):
+            emu.mm_nt(A, Bt)                          # eager calls first: they create the library streams
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            got = emu.mm_nt(A, Bt)
+        A.copy_(torch.randn(1100, 500, dtype=torch.float64, device="cuda"))
+        Bt.copy_(torch.randn(500, 260, dtype=torch.float64, device="cuda"))
+        g.replay()
+        torch.cuda.synchronize()
+        want = emu.mm_nt(A, Bt)
+    with chunk(0):
+        flat = emu.mm_nt(A, Bt)
+    torch.cuda.synchronize()
+    assert torch.equal(got, want)
+    assert torch.equal(got, flat)

@@ -189,7 +189,8 @@ class Step:
         self.fp64_emu = fp64_emu
 
     def new_events(self):
-        ev = [torch.cuda.Event(enable_timing=True) for _ in range(2 * self.MAX_LAUNCHES)]
+        """Step-start event + two events per possible GEMM launch."""
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(1 + 2 * self.MAX_LAUNCHES)]
         for e in ev:
             e.record()   # creates the underlying CUDA event
         return ev
@@ -197,16 +198,27 @@ class Step:
     def run(self, events=None):
         """Returns the number of GEMM launches of the step."""
         sp, out = self.sp, self.out
+        if events is not None:
+            events[0].record()
         sp.sizing(out)
         if events is None:
             sp._phase(out, 14)
             return 0
         return self.fp64_emu.ops.fp64_emu_gemm_ws_ev(out, sp.ws, sp.A, sp.B, sp.primes, sp.b_kn, sp.exact, sp.bits,
-                                                     sp.corr, 14, sp.slab_cols, [e.cuda_event for e in events])
+                                                     sp.corr, 14, sp.slab_cols, [e.cuda_event for e in events[1:]])
 
     @staticmethod
     def gemm_ms(events, launches):
-        return sum(events[2 * i].elapsed_time(events[2 * i + 1]) for i in range(launches))
+        """Time during which at least one GEMM launch of the step ran (chunks on
+        two streams overlap at their boundaries)."""
+        t0 = events[0]
+        iv = sorted((t0.elapsed_time(events[1 + 2 * i]), t0.elapsed_time(events[2 + 2 * i])) for i in range(launches))
+        busy, end = 0.0, float("-inf")
+        for a, b in iv:
+            if b > end:
+                busy += b - max(a, end)
+                end = b
+        return busy
 
 
 def barrier():

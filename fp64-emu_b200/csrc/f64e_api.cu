@@ -299,21 +299,27 @@ int run_sizing(const Plan& l, const double* A, const double* B, void* ws, cudaSt
 }
 
 // A view of the product: the whole problem, or one chunk of it (a block of
-// rows of A and C for a single product, a block of members for a batch).  Each
-// chunk owns a contiguous share of every intermediate buffer in the chunk's
-// own layout ([G][members][rows][Kp] planes, [P][members * rows][ldn]
-// residues), so the kernels see it as a product of its own.
+// rows of A and C, a block of rows and columns of the first row block, or a
+// block of members of a batch).  Each chunk owns a contiguous share of the
+// residue buffers and of A's planes in the chunk's own layout
+// ([G][members][rows][Kp] planes, [P][members * rows][ldn] residues), so the
+// kernels see it as a product of its own.  B's planes stay in the whole
+// product's layout for row and column blocks (a column block addresses a
+// band of rows of every plane) and are per chunk for member blocks.
 struct View {
-  int64_t batch, M;            // members and rows of A / C in this view
+  int64_t batch, M, N;         // members, rows of A / C, columns of C in this view
+  int64_t ldn;                 // row pitch of this view's residues
+  int64_t ldc;                 // row pitch of C
+  int64_t b_zrows;             // rows from one B plane slice (plane, member) to the next
   const double* A;             // [batch][M][K]
-  const double* B;             // [batch][N][K] or [batch][K][N]
+  const double* B;             // first of this view's rows ([N][K] layout) or columns ([K][N] layout)
   const int16_t* sftA;         // [batch * M]
   const int16_t* sftB;         // [batch * N]
   int8_t* pA;                  // [G][batch][M][Kp]
-  int8_t* pB;                  // [G][batch][N][Kp]
+  int8_t* pB;                  // B planes: slice z at pB + z * b_zrows * Kp
   int8_t* res;                 // [P][batch * M][ldn]
   int32_t* corr;               // [ncorr][batch * M][ldn]
-  double* C;                   // [batch * M][N]
+  double* C;                   // [batch * M] rows of pitch ldc
 };
 
 int ncorr_planes(const Plan& l) { return l.gemm_corr == 2 ? 2 : (l.gemm_corr == 1 ? 1 : 0); }
@@ -322,6 +328,10 @@ View full_view(const Plan& l, const double* A, const double* B, void* ws, double
   View v;
   v.batch = l.batch;
   v.M = l.M;
+  v.N = l.N;
+  v.ldn = l.ldn;
+  v.ldc = l.N;
+  v.b_zrows = l.N;
   v.A = A;
   v.B = B;
   v.sftA = at<int16_t>(ws, l.o_sftA);
@@ -334,7 +344,7 @@ View full_view(const Plan& l, const double* A, const double* B, void* ws, double
   return v;
 }
 
-// Rows [r0, r1) of a single product (B shared by every chunk).
+// Rows [r0, r1) of a single product (B's planes shared by every chunk).
 View row_chunk(const Plan& l, const View& f, int64_t r0, int64_t r1) {
   View v = f;
   v.M = r1 - r0;
@@ -344,6 +354,22 @@ View row_chunk(const Plan& l, const View& f, int64_t r0, int64_t r1) {
   v.res = f.res + (int64_t)l.P * r0 * l.ldn;
   v.corr = f.corr + (int64_t)ncorr_planes(l) * r0 * l.ldn;
   v.C = f.C + r0 * l.N;
+  return v;
+}
+
+// Columns [c0, c1) of a row chunk r of a single product; `before` is the sum
+// of the residue pitches of the chunk's earlier column blocks, so the blocks
+// tile the chunk's residue share.
+View col_block(const Plan& l, const View& r, int64_t c0, int64_t c1, int64_t before) {
+  View v = r;
+  v.N = c1 - c0;
+  v.ldn = round_up(v.N, 16);
+  v.B = r.B + (l.nt ? c0 : c0 * l.K);
+  v.sftB = r.sftB + c0;
+  v.pB = r.pB + c0 * l.Kp;
+  v.res = r.res + (int64_t)l.P * r.M * before;
+  v.corr = r.corr + (int64_t)ncorr_planes(l) * r.M * before;
+  v.C = r.C + c0;
   return v;
 }
 
@@ -369,7 +395,6 @@ ExtractArgs extract_args(const Plan& l, void* ws, int64_t k0, int64_t kw) {
   ea.Kp = l.Kp;
   ea.ld = l.K;
   ea.koff = k0;
-  ea.N = l.N;
   ea.maxlg = at<WsHead>(ws, 0)->maxlg;
   ea.bits = l.bits;
   ea.use_corr = l.use_corr;
@@ -382,10 +407,12 @@ void extract_A(const Plan& l, const ModTables& T, const View& v, void* ws, int64
   ea.X = v.A;
   ea.rows = v.batch * v.M;
   ea.batch = v.batch;
+  ea.N = v.N;
   ea.sft = v.sftA;
   ea.hi_plane = l.P;
   ea.q_plane = l.P + 1;
   ea.planes = v.pA;
+  ea.pstride = ea.rows * l.Kp;
   launch_extract_rows(ea, T, s);
 }
 
@@ -393,12 +420,15 @@ void extract_A(const Plan& l, const ModTables& T, const View& v, void* ws, int64
 void extract_B(const Plan& l, const ModTables& T, const View& v, void* ws, int64_t k0, int64_t kw, cudaStream_t s) {
   ExtractArgs eb = extract_args(l, ws, k0, kw);
   eb.X = v.B;
-  eb.rows = v.batch * l.N;
+  eb.rows = v.batch * v.N;
   eb.batch = v.batch;
+  eb.N = v.N;
+  if (l.nt) eb.ld = l.N;   // [K][N]: row pitch of the whole operand
   eb.sft = v.sftB;
   eb.q_plane = l.P;
   eb.hi_plane = l.P + 1;
   eb.planes = v.pB;
+  eb.pstride = v.batch * v.b_zrows * l.Kp;
   if (l.nt) launch_extract_cols(eb, T, s);
   else launch_extract_rows(eb, T, s);
 }
@@ -406,13 +436,13 @@ void extract_B(const Plan& l, const ModTables& T, const View& v, void* ws, int64
 GemmArgs gemm_args(const Plan& l, const View& v, void* ws) {
   GemmArgs g{};
   g.M = (int)v.M;
-  g.N = (int)l.N;
+  g.N = (int)v.N;
   g.batch = (int)v.batch;
   g.P = l.P;
   g.Kp = (int)l.Kp;
   g.nkb = (int)((l.Kp + 127) / 128);
   g.corr_mode = l.gemm_corr;
-  g.ldn = (int)l.ldn;
+  g.ldn = (int)v.ldn;
   g.res = v.res;
   g.corr = v.corr;
   g.status = &at<WsHead>(ws, 0)->status;
@@ -426,7 +456,7 @@ int gemm_maps(const Plan& l, const View& v, CUtensorMap* tA, CUtensorMap* tB) {
   const int rows_a = pair ? gemm_pair_block_rows() : gemm_block_rows_a();
   const int rows_b = pair ? gemm_pair_block_rows() : gemm_block_rows_b();
   if (!encode_plane_map(tA, v.pA, (int64_t)l.G * v.batch, v.M, l.Kp, rows_a) ||
-      !encode_plane_map(tB, v.pB, (int64_t)l.G * v.batch, l.N, l.Kp, rows_b))
+      !encode_plane_map(tB, v.pB, (int64_t)l.G * v.batch, v.N, l.Kp, rows_b, v.b_zrows))
     return fail(F64E_ERR_CUDA, "cuTensorMapEncodeTiled rejected the plane layout");
   return F64E_OK;
 }
@@ -444,7 +474,7 @@ int launch_gemm_view(const Plan& l, const ModTables& T, const View& v, const CUt
 int run_gemm(const Plan& l, const ModTables& T, const View& v, void* ws, const Dev& d, bool checked, cudaStream_t s) {
   if (checked) {
     const GemmArgs g = gemm_args(l, v, ws);
-    launch_residue_gemm_check(v.pA, v.pB, v.batch * v.M, v.batch * l.N, g, T, s);
+    launch_residue_gemm_check(v.pA, v.pB, v.batch * v.M, v.batch * v.N, g, T, s);
     const cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(e, "modular GEMM launch");
     return F64E_OK;
@@ -463,31 +493,38 @@ void run_reconstruct(const Plan& l, const ModTables& T, const View& v, void* ws,
   r.corr = corr;
   r.MF = v.batch * v.M;
   r.M = v.M;
-  r.N = l.N;
-  r.ldn = l.ldn;
+  r.N = v.N;
+  r.ldn = v.ldn;
   r.sftA = v.sftA;
   r.sftB = v.sftB;
   r.maxlg = at<WsHead>(ws, 0)->maxlg;
   r.bits = l.bits;
   r.exact = l.exact;
   r.C = v.C;
+  r.ldc = v.ldc;
   launch_reconstruct(r, T, s);
 }
 
 // ------------------------------------------------------------ pipelining --
-// A product whose three compute phases run in one call is cut into chunks
-// (rows of A and C, or members of a batch).  The GEMM of chunk c runs on a
-// high-priority library stream while the extraction of later chunks (a
-// low-priority library stream) and the reconstruction of earlier ones (the
-// caller's stream) share the SMs with it: the persistent GEMM holds one CTA
-// per SM and leaves registers for one block of either kernel.  Results are
-// the same bits as the unchunked product: every element's arithmetic is
-// independent of the chunking and the sizing covers the whole product.
+// A product whose three compute phases run in one call is cut into chunks.
+// A single product is cut into row blocks, and its first row block again
+// into column blocks, so the first GEMM needs only a slice of each operand
+// extracted: the extraction exposed before the pipeline fills is one row
+// block of A and one column block of B.  A batch is cut into member blocks.
+// GEMM chunks run on two high-priority library streams in turn (chunk c + 1
+// takes each SM as soon as chunk c's CTA there exits), the extraction of
+// later chunks on a low-priority library stream and the reconstruction of
+// earlier ones on the caller's stream: the persistent GEMM holds one CTA per
+// SM and leaves registers and shared memory for one block of either kernel
+// beside it.  Results are the same bits as the unchunked product: every
+// element's arithmetic is independent of the chunking and the sizing covers
+// the whole product.
 constexpr int kPipeMaxChunks = 16;
-constexpr int kPipeEvents = 2 * kPipeMaxChunks + 2;
+constexpr int kPipeMaxCols = 4;
+constexpr int kPipeEvents = 4 * (kPipeMaxChunks + kPipeMaxCols) + 4;
 
 struct PipeRes {
-  cudaStream_t hi = nullptr, aux = nullptr;
+  cudaStream_t hi[2] = {nullptr, nullptr}, aux = nullptr;
   cudaEvent_t ev[kPipeEvents] = {};
   std::mutex mtx;
 };
@@ -507,7 +544,7 @@ PipeRes* pipe_res(int dev, cudaStream_t s, int* rc) {
   int lo = 0, hi = 0;
   cudaError_t e = cudaDeviceGetStreamPriorityRange(&lo, &hi);
   PipeRes* r = new PipeRes;
-  if (e == cudaSuccess) e = cudaStreamCreateWithPriority(&r->hi, cudaStreamNonBlocking, hi);
+  for (int i = 0; i < 2 && e == cudaSuccess; i++) e = cudaStreamCreateWithPriority(&r->hi[i], cudaStreamNonBlocking, hi);
   if (e == cudaSuccess) e = cudaStreamCreateWithPriority(&r->aux, cudaStreamNonBlocking, lo);
   for (int i = 0; i < kPipeEvents && e == cudaSuccess; i++) e = cudaEventCreateWithFlags(&r->ev[i], cudaEventDisableTiming);
   if (e != cudaSuccess) {
@@ -519,76 +556,128 @@ PipeRes* pipe_res(int dev, cudaStream_t s, int* rc) {
 }
 
 // F64E_PIPE_CHUNK=<n> sets the chunk extent (rows of a single product,
-// members of a batch) and F64E_PIPE_CHUNK=0 turns chunking off; read per
-// call (A/B checks of the chunked path against the unchunked one).
-int64_t pipe_chunk_override() {
-  const char* v = std::getenv("F64E_PIPE_CHUNK");
+// members of a batch) and F64E_PIPE_CHUNK=0 turns chunking off;
+// F64E_PIPE_COLS=<n> sets the column block of the first row block (0: none).
+// Read per call (A/B checks of the chunked path against the unchunked one).
+int64_t env_int(const char* name) {
+  const char* v = std::getenv(name);
   if (!v || !*v) return -1;
   return std::max<int64_t>(0, std::atoll(v));
 }
 
-// Chunk extent for a product, 0 when it runs unchunked.
-int64_t pipe_chunk(const Plan& l, bool* by_batch) {
-  *by_batch = l.batch > 1;
-  const int64_t extent = *by_batch ? l.batch : l.M;
-  int64_t per = 0;
-  const int64_t ov = pipe_chunk_override();
+struct Chunking {
+  bool by_batch = false;
+  int64_t per = 0;    // rows (or members) per chunk; 0 = unchunked
+  int64_t cols = 0;   // columns per block of the first row chunk; 0 = whole
+};
+
+Chunking pipe_chunking(const Plan& l) {
+  Chunking c;
+  c.by_batch = l.batch > 1;
+  const int64_t extent = c.by_batch ? l.batch : l.M;
+  const int64_t ov = env_int("F64E_PIPE_CHUNK");
   if (ov >= 0) {
-    per = ov;
-  } else if (*by_batch) {
-    // members of 2048 or more rows in all, eight chunks at most
-    if (l.MF >= 2048 && l.batch >= 4) per = (l.batch + 7) / 8;
+    c.per = ov;
+  } else if (c.by_batch) {
+    // member blocks of 2048 or more rows in all, eight chunks at most
+    if (l.MF >= 2048 && l.batch >= 4) c.per = (l.batch + 7) / 8;
   } else if (l.M >= 2048) {
-    const int64_t n = std::min<int64_t>(8, l.M / 1024);
-    per = round_up((l.M + n - 1) / n, 256);
+    // row chunks of about 2048 rows (at least two, eight at most): shorter
+    // chunks leave the extraction of the next one less GEMM time to hide in
+    const int64_t n = std::min<int64_t>(8, std::max<int64_t>(2, l.M / 2048));
+    c.per = round_up((l.M + n - 1) / n, 256);
   }
-  if (per <= 0 || per >= extent) return 0;
-  if ((extent + per - 1) / per > kPipeMaxChunks) per = (extent + kPipeMaxChunks - 1) / kPipeMaxChunks;
-  return per;
+  if (c.per <= 0 || c.per >= extent) {
+    c.per = 0;
+    return c;
+  }
+  if ((extent + c.per - 1) / c.per > kPipeMaxChunks) c.per = (extent + kPipeMaxChunks - 1) / kPipeMaxChunks;
+  if (!c.by_batch) {
+    // Column blocks of the first row chunk shorten the exposed extraction,
+    // but their GEMMs are too short to hide the next block's extraction on
+    // B200 (measured: net loss at 8192^3), so they stay off unless asked for.
+    const int64_t cv = env_int("F64E_PIPE_COLS");
+    if (cv >= 0) c.cols = cv;
+    if (c.cols > 0) c.cols = std::max<int64_t>(c.cols, (l.N + kPipeMaxCols - 1) / kPipeMaxCols);
+    if (c.cols > 0) c.cols = round_up(c.cols, 16);
+    if (c.cols >= l.N) c.cols = 0;
+  }
+  return c;
 }
 
 int run_pipelined(const Plan& l, const ModTables& T, const View& f, void* ws, const Dev& d, PipeRes* pr,
-                  int64_t per, bool by_batch, cudaStream_t s, void* const* gev, int ngev, int* launches) {
-  const int64_t extent = by_batch ? l.batch : l.M;
-  const int C = (int)((extent + per - 1) / per);
-  std::vector<View> v(C);
-  std::vector<CUtensorMap> tA(C), tB(C);
+                  const Chunking& ch, cudaStream_t s, void* const* gev, int ngev, int* launches) {
+  const int64_t extent = ch.by_batch ? l.batch : l.M;
+  const int C = (int)((extent + ch.per - 1) / ch.per);
+  // GEMM units in launch order: the column blocks of row chunk 0, then row chunks 1.. (or member chunks).
+  std::vector<View> rows(C), units;
   for (int c = 0; c < C; c++) {
-    const int64_t a0 = c * per, a1 = std::min(extent, a0 + per);
-    v[c] = by_batch ? batch_chunk(l, f, a0, a1) : row_chunk(l, f, a0, a1);
-    const int rc = gemm_maps(l, v[c], &tA[c], &tB[c]);   // all host-side failures before the first launch
+    const int64_t a0 = c * ch.per, a1 = std::min(extent, a0 + ch.per);
+    rows[c] = ch.by_batch ? batch_chunk(l, f, a0, a1) : row_chunk(l, f, a0, a1);
+  }
+  const int J = ch.cols > 0 ? (int)((l.N + ch.cols - 1) / ch.cols) : 1;
+  std::vector<View> bcols(J, f);   // B column blocks (their extraction views)
+  if (J > 1) {
+    int64_t before = 0;
+    for (int j = 0; j < J; j++) {
+      const int64_t c0 = j * ch.cols, c1 = std::min(l.N, c0 + ch.cols);
+      units.push_back(col_block(l, rows[0], c0, c1, before));
+      bcols[j] = units.back();
+      before += round_up(c1 - c0, 16);
+    }
+  } else {
+    units.push_back(rows[0]);
+  }
+  for (int c = 1; c < C; c++) units.push_back(rows[c]);
+  const int U = (int)units.size();
+  std::vector<CUtensorMap> tA(U), tB(U);
+  for (int u = 0; u < U; u++) {
+    const int rc = gemm_maps(l, units[u], &tA[u], &tB[u]);   // all host-side failures before the first launch
     if (rc) return rc;
   }
+  // need[u]: index of the extraction event GEMM unit u waits for (-1: extracted before the fork)
+  std::vector<int> need(U, -1);
   std::lock_guard<std::mutex> lk(pr->mtx);
-  cudaEvent_t* E = pr->ev;   // E[0] fork, E[c] chunk c extracted, E[C + c] chunk c multiplied, E[2C] aux done
-  if (!by_batch) extract_B(l, T, f, ws, 0, l.K, s);
-  extract_A(l, T, v[0], ws, 0, l.K, s);
-  if (by_batch) extract_B(l, T, v[0], ws, 0, l.K, s);
+  cudaEvent_t* E = pr->ev;
+  int ne = 1;   // E[0] = fork
+  // Head, on the caller's stream: everything the first GEMM unit reads.
+  extract_A(l, T, rows[0], ws, 0, l.K, s);
+  if (ch.by_batch) extract_B(l, T, rows[0], ws, 0, l.K, s);
+  else extract_B(l, T, J > 1 ? bcols[0] : f, ws, 0, l.K, s);
   cudaError_t e = cudaEventRecord(E[0], s);
-  if (e == cudaSuccess) e = cudaStreamWaitEvent(pr->hi, E[0], 0);
+  for (int i = 0; i < 2 && e == cudaSuccess; i++) e = cudaStreamWaitEvent(pr->hi[i], E[0], 0);
   if (e == cudaSuccess) e = cudaStreamWaitEvent(pr->aux, E[0], 0);
   if (e != cudaSuccess) return cuda_fail(e, "pipeline fork");
+  // The rest of the extraction, in the order the GEMM units need it.
+  for (int j = 1; j < J; j++) {
+    extract_B(l, T, bcols[j], ws, 0, l.K, pr->aux);
+    cudaEventRecord(E[ne], pr->aux);
+    need[j] = ne++;
+  }
   for (int c = 1; c < C; c++) {
-    extract_A(l, T, v[c], ws, 0, l.K, pr->aux);
-    if (by_batch) extract_B(l, T, v[c], ws, 0, l.K, pr->aux);
-    cudaEventRecord(E[c], pr->aux);
+    extract_A(l, T, rows[c], ws, 0, l.K, pr->aux);
+    if (ch.by_batch) extract_B(l, T, rows[c], ws, 0, l.K, pr->aux);
+    cudaEventRecord(E[ne], pr->aux);
+    need[(J > 1 ? J : 1) + c - 1] = ne++;
   }
-  cudaEventRecord(E[2 * C], pr->aux);
+  const int e_aux = ne++;
+  cudaEventRecord(E[e_aux], pr->aux);
   int rc = F64E_OK;
-  for (int c = 0; c < C; c++) {
-    if (c > 0) cudaStreamWaitEvent(pr->hi, E[c], 0);
-    if (2 * c + 1 < ngev) cudaEventRecord(static_cast<cudaEvent_t>(gev[2 * c]), pr->hi);
-    if (rc == F64E_OK) rc = launch_gemm_view(l, T, v[c], tA[c], tB[c], ws, d, pr->hi);
-    if (2 * c + 1 < ngev) cudaEventRecord(static_cast<cudaEvent_t>(gev[2 * c + 1]), pr->hi);
-    cudaEventRecord(E[C + c], pr->hi);
+  const int e_gemm = ne;
+  for (int u = 0; u < U; u++) {
+    cudaStream_t h = pr->hi[u & 1];
+    if (need[u] >= 0) cudaStreamWaitEvent(h, E[need[u]], 0);
+    if (2 * u + 1 < ngev) cudaEventRecord(static_cast<cudaEvent_t>(gev[2 * u]), h);
+    if (rc == F64E_OK) rc = launch_gemm_view(l, T, units[u], tA[u], tB[u], ws, d, h);
+    if (2 * u + 1 < ngev) cudaEventRecord(static_cast<cudaEvent_t>(gev[2 * u + 1]), h);
+    cudaEventRecord(E[e_gemm + u], h);
   }
-  const int cm = l.recon_corr;
-  for (int c = 0; c < C; c++) {
-    cudaStreamWaitEvent(s, E[C + c], 0);
-    run_reconstruct(l, T, v[c], ws, cm, v[c].corr, s);
+  for (int u = 0; u < U; u++) {
+    cudaStreamWaitEvent(s, E[e_gemm + u], 0);   // joins both GEMM streams
+    run_reconstruct(l, T, units[u], ws, l.recon_corr, units[u].corr, s);
   }
-  e = cudaStreamWaitEvent(s, E[2 * C], 0);   // join the extraction stream
-  if (launches) *launches = C;
+  e = cudaStreamWaitEvent(s, E[e_aux], 0);      // joins the extraction stream
+  if (launches) *launches = U;
   if (rc) return rc;
   if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "pipelined launch");
@@ -630,12 +719,11 @@ int run(const f64e_problem* p, const double* A, const double* B, double* out, vo
   if (!(phases & F64E_PHASE_COMPUTE)) return F64E_OK;
   const View f = full_view(l, A, B, ws, out);
   if (!ev && !checked && !l.deep && (phases & F64E_PHASE_COMPUTE) == F64E_PHASE_COMPUTE) {
-    bool by_batch = false;
-    const int64_t per = pipe_chunk(l, &by_batch);
-    if (per > 0) {
+    const Chunking ch = pipe_chunking(l);
+    if (ch.per > 0) {
       PipeRes* pr = pipe_res(d.dev, s, &rc);
       if (rc) return rc;
-      if (pr) return run_pipelined(l, T, f, ws, d, pr, per, by_batch, s, gev, ngev, launches);
+      if (pr) return run_pipelined(l, T, f, ws, d, pr, ch, s, gev, ngev, launches);
     }
   }
   if (!l.deep) {

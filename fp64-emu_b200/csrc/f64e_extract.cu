@@ -182,7 +182,7 @@ __global__ void __launch_bounds__(256) extract_rows_kernel(const ExtractArgs a, 
   const bool corr = a.use_corr != 0;
   const int P = T.P;
   const int64_t nch = a.Kp >> 3;
-  const int64_t pstride = a.rows * a.Kp;
+  const int64_t pstride = a.pstride;
   for (int64_t r = (int64_t)blockIdx.y * 8 + threadIdx.y; r < a.rows; r += (int64_t)gridDim.y * 8) {
     const int s = (int)a.sft[r] + gn.g;
     const bool row_fast = (s >= -960) && (s <= 960);
@@ -241,17 +241,66 @@ __global__ void __launch_bounds__(256) extract_rows_kernel(const ExtractArgs a, 
 
 // [batch, K, N] operand: a block transposes a 64 (k) x 32 (n) tile.  Thread
 // (n = lane, warp w) reads columns coalesced along n for the k quads w and
-// w + 8, packs four k-consecutive residues per plane into one word in shared
-// memory (row pitch 17 words: conflict-free writes), then the block writes
-// each plane's 32 x 64-byte tile as 16-byte vectors along K.
-constexpr int kColTileK = 64, kColTileN = 32, kColPitch = 17;
+// w + 8 and splits its eight elements once; then, for each group of up to 11
+// planes, it packs four k-consecutive residues per plane into one word in
+// shared memory (row pitch 17 words: conflict-free writes) and the block
+// writes each plane's 32 x 64-byte tile as 16-byte vectors along K.  Two
+// plane groups keep the block at 24 KB of shared memory, so it runs beside a
+// resident GEMM CTA.
+constexpr int kColTileK = 64, kColTileN = 32, kColPitch = 17, kColGroup = 11;
+static_assert(2 * kColGroup >= kMaxP + 2, "two plane groups cover every plane");
+
+template <int T0>
+__device__ __forceinline__ void cols_fill_group(uint32_t (*sw)[kColTileN][kColPitch], const Split (&S)[2][4],
+                                                const bool (&ok)[2], const ExtractArgs& a, const ModTables& T,
+                                                int be, bool corr, int tx, int ty) {
+  const int P = T.P;
+#pragma unroll
+  for (int qi = 0; qi < 2; qi++) {
+    const int qd = ty + 8 * qi;
+    if (ok[qi]) {
+#pragma unroll
+      for (int tt = 0; tt < kColGroup; tt++) {
+        const int t = T0 + tt;
+        if (t >= P || t >= kMaxP) break;
+        uint32_t w[1];
+        residue_words<4>(S[qi], T, t, be, w);
+        sw[tt][tx][qd] = w[0];
+      }
+    } else {
+      for (int t = T0; t < min(P, T0 + kColGroup); t++) {
+        const uint32_t p = T.p[t], cb = p - (uint32_t)T.pow2mod[t][be - 16];
+        sw[t - T0][tx][qd] = residue_word_ref(S[qi][0].u, S[qi][1].u, S[qi][2].u, S[qi][3].u, p, T.c36[t], T.c18[t],
+                                              cb, T.mu2[t]);
+      }
+    }
+    if (corr) {
+      if (a.hi_plane >= T0 && a.hi_plane < T0 + kColGroup)
+        sw[a.hi_plane - T0][tx][qd] = pack4i(S[qi][0].h, S[qi][1].h, S[qi][2].h, S[qi][3].h);
+      if (a.q_plane >= T0 && a.q_plane < T0 + kColGroup)
+        sw[a.q_plane - T0][tx][qd] = pack4i(S[qi][0].q, S[qi][1].q, S[qi][2].q, S[qi][3].q);
+    }
+  }
+}
+
+__device__ __forceinline__ void cols_write_group(uint32_t (*sw)[kColTileN][kColPitch], const ExtractArgs& a, int t0,
+                                                 int nt, int64_t b, int64_t n0, int64_t k0) {
+  for (int i = threadIdx.x; i < nt * 128; i += 256) {
+    const int tt = i >> 7, rem = i & 127, row = rem >> 2, part = rem & 3;
+    const int64_t nn = n0 + row, kk = k0 + part * 16;
+    if (nn < a.N && kk < a.Kp) {
+      const uint4 v = make_uint4(sw[tt][row][part * 4 + 0], sw[tt][row][part * 4 + 1], sw[tt][row][part * 4 + 2],
+                                 sw[tt][row][part * 4 + 3]);
+      *reinterpret_cast<uint4*>(a.planes + (t0 + tt) * a.pstride + (b * a.N + nn) * a.Kp + kk) = v;
+    }
+  }
+}
 
 __global__ void __launch_bounds__(256) extract_cols_kernel(const ExtractArgs a, const ModTables T) {
-  __shared__ uint32_t sw[kMaxP + 2][kColTileN][kColPitch];
+  __shared__ uint32_t sw[kColGroup][kColTileN][kColPitch];
   const Gain gn = pick_gain(a.maxlg[0], a.maxlg[1], T.log2M, a.bits);
   const int be = gn.bits_eff;
   const bool corr = a.use_corr != 0;
-  const int P = T.P;
   const int64_t b = blockIdx.z;
   const int64_t n0 = (int64_t)blockIdx.x * kColTileN, k0 = (int64_t)blockIdx.y * kColTileK;
   const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
@@ -260,50 +309,30 @@ __global__ void __launch_bounds__(256) extract_cols_kernel(const ExtractArgs a, 
   const int s = nin ? (int)a.sft[b * a.N + n] + gn.g : 0;
   const bool col_fast = (s >= -960) && (s <= 960);
   const double p2s = pow2d(col_fast ? s : 0), p2h = pow2d(7 - be);
-  const double* __restrict__ xb = a.X + b * a.K * a.N + n;
+  const double* __restrict__ xb = a.X + b * a.K * a.ld + n;   // row pitch a.ld (>= a.N)
+  Split S[2][4];
+  bool ok[2];
 #pragma unroll
   for (int qi = 0; qi < 2; qi++) {
-    const int qd = ty + 8 * qi;
-    const int64_t kb = k0 + 4 * qd;
-    Split S[4];
-    bool ok = true;
+    const int64_t kb = k0 + 4 * (ty + 8 * qi);
+    ok[qi] = true;
 #pragma unroll
     for (int u = 0; u < 4; u++) {
       const int64_t k = kb + u;
-      const double x = (nin && k < a.K) ? __ldg(xb + k * a.N) : 0.0;
-      if (!(col_fast && split_fast(x, p2s, p2h, be, corr, S[u]))) S[u] = split_slow(x, s, be, corr);
-      ok = ok && (S[u].u >> 56) == 0;
-    }
-    if (ok) {
-#pragma unroll
-      for (int t = 0; t < kMaxP; t++) {
-        if (t >= P) break;
-        uint32_t w[1];
-        residue_words<4>(S, T, t, be, w);
-        sw[t][tx][qd] = w[0];
-      }
-    } else {
-      for (int t = 0; t < P; t++) {
-        const uint32_t p = T.p[t], cb = p - (uint32_t)T.pow2mod[t][be - 16];
-        sw[t][tx][qd] = residue_word_ref(S[0].u, S[1].u, S[2].u, S[3].u, p, T.c36[t], T.c18[t], cb, T.mu2[t]);
-      }
-    }
-    if (corr) {
-      sw[a.hi_plane][tx][qd] = pack4i(S[0].h, S[1].h, S[2].h, S[3].h);
-      sw[a.q_plane][tx][qd] = pack4i(S[0].q, S[1].q, S[2].q, S[3].q);
+      const double x = (nin && k < a.K) ? __ldg(xb + k * a.ld) : 0.0;
+      if (!(col_fast && split_fast(x, p2s, p2h, be, corr, S[qi][u]))) S[qi][u] = split_slow(x, s, be, corr);
+      ok[qi] = ok[qi] && (S[qi][u].u >> 56) == 0;
     }
   }
+  const int G = T.P + (corr ? 2 : 0);
+  cols_fill_group<0>(sw, S, ok, a, T, be, corr, tx, ty);
   __syncthreads();
-  const int G = P + (corr ? 2 : 0);
-  const int64_t pstride = a.rows * a.Kp;
-  for (int i = threadIdx.x; i < G * 128; i += 256) {
-    const int t = i >> 7, rem = i & 127, row = rem >> 2, part = rem & 3;
-    const int64_t nn = n0 + row, kk = k0 + part * 16;
-    if (nn < a.N && kk < a.Kp) {
-      const uint4 v = make_uint4(sw[t][row][part * 4 + 0], sw[t][row][part * 4 + 1], sw[t][row][part * 4 + 2],
-                                 sw[t][row][part * 4 + 3]);
-      *reinterpret_cast<uint4*>(a.planes + t * pstride + (b * a.N + nn) * a.Kp + kk) = v;
-    }
+  cols_write_group(sw, a, 0, min(G, kColGroup), b, n0, k0);
+  if (G > kColGroup) {
+    __syncthreads();
+    cols_fill_group<kColGroup>(sw, S, ok, a, T, be, corr, tx, ty);
+    __syncthreads();
+    cols_write_group(sw, a, kColGroup, G - kColGroup, b, n0, k0);
   }
 }
 

@@ -470,7 +470,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 
 // 3-D tensor map over K-major planes [zdim][rows][Kp] (uint8), box
 // (128 bytes of K) x box_rows x 1, 128-byte swizzle, zero fill outside.
-bool encode_plane_map(CUtensorMap* map, const void* base, int64_t zdim, int64_t rows, int64_t Kp, int box_rows) {
+bool encode_plane_map(CUtensorMap* map, const void* base, int64_t zdim, int64_t rows, int64_t Kp, int box_rows,
+                      int64_t zrows) {
   using EncodeFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                 const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
                                 CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
@@ -484,7 +485,7 @@ bool encode_plane_map(CUtensorMap* map, const void* base, int64_t zdim, int64_t 
   }();
   if (!fn) return false;
   const cuuint64_t gdim[3] = {(cuuint64_t)Kp, (cuuint64_t)rows, (cuuint64_t)zdim};
-  const cuuint64_t gstride[2] = {(cuuint64_t)Kp, (cuuint64_t)(rows * Kp)};
+  const cuuint64_t gstride[2] = {(cuuint64_t)Kp, (cuuint64_t)((zrows > 0 ? zrows : rows) * Kp)};
   const cuuint32_t box[3] = {(cuuint32_t)BK, (cuuint32_t)box_rows, 1};
   const cuuint32_t estride[3] = {1, 1, 1};
   return fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(base), gdim, gstride, box, estride,

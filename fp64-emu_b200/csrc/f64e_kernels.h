@@ -21,15 +21,17 @@ void launch_col_stats(const double* X, int64_t batch, int64_t K, int64_t N, int6
 void launch_maxlg(const float* lgA, int64_t m, const float* lgB, int64_t n, float* out, cudaStream_t s);
 
 // ---- extraction (f64e_extract.cu) ----
-// Planes are K-major int8: plane t of an operand with `rows` rows lives at
-// planes + t * rows * Kp, row r at + r * Kp, Kp = K rounded up to 16 (the pad
-// columns are written as zeros).  Plane order: residues 0..P-1, then the two
+// Planes are K-major int8: plane t lives at planes + t * pstride (rows * Kp
+// for an operand's own planes; more for a block of rows of larger planes),
+// row r at + r * Kp, Kp = K rounded up to 16 (the pad columns are written as
+// zeros).  Plane order: residues 0..P-1, then the two
 // correction planes at P and P + 1, whose roles (hi or q) the caller picks.
 struct ExtractArgs {
   const double* X;      // operand
   int64_t rows;         // rows of the K-major planes (batch * M, or batch * N)
   int64_t K, Kp;        // extracted K window and plane pitch
-  int64_t ld, koff;     // [rows, K] layout: element (r, k) at X[r * ld + koff + k]
+  int64_t ld, koff;     // [rows, K] layout: element (r, k) at X[r * ld + koff + k];
+                        // [K, N] layout: element (k, n) of member b at X[(b * K + k) * ld + n]
   int64_t batch, N;     // [K, N] layout only: members and columns per member
   const int16_t* sft;   // per-row (or per-column) shifts before widening
   const float* maxlg;   // operand maxima of lg (WsHead::maxlg)
@@ -37,6 +39,7 @@ struct ExtractArgs {
   int use_corr;
   int hi_plane, q_plane;  // plane indices of the correction digits
   int8_t* planes;
+  int64_t pstride;      // bytes from one plane to the next
 };
 void launch_extract_rows(const ExtractArgs& a, const ModTables& T, cudaStream_t s);  // X is [rows, K]
 void launch_extract_cols(const ExtractArgs& a, const ModTables& T, cudaStream_t s);  // X is [batch, K, N]
@@ -53,7 +56,10 @@ struct GemmArgs {
   int* status;
   uint64_t wait_limit_ns;
 };
-bool encode_plane_map(CUtensorMap* map, const void* base, int64_t zdim, int64_t rows, int64_t Kp, int box_rows);
+// 3-D map (Kp, rows, zdim) of K-major int8 planes; consecutive z-slices are
+// zrows * Kp bytes apart (zrows = rows when 0).
+bool encode_plane_map(CUtensorMap* map, const void* base, int64_t zdim, int64_t rows, int64_t Kp, int box_rows,
+                      int64_t zrows = 0);
 int gemm_block_rows_a();
 int gemm_block_rows_b();
 int gemm_pair_block_rows();   // box rows of both operands in the CTA-pair kernel
@@ -79,7 +85,8 @@ struct ReconArgs {
   const int16_t* sftB;   // [batch * N], before widening
   const float* maxlg;
   int bits, exact;
-  double* C;             // [batch * M][N]
+  double* C;             // [batch * M][N], row pitch ldc
+  int64_t ldc;
 };
 void launch_reconstruct(const ReconArgs& a, const ModTables& T, cudaStream_t s);
 

@@ -131,7 +131,7 @@ __global__ void __launch_bounds__(256) reconstruct_kernel(const ReconArgs a, con
   const int ng = (P + 6) / 7;
   const int64_t nq = (a.N + 3) >> 2;
   const int64_t plane = a.MF * a.ldn;
-  const bool vec_out = ((a.N & 3) == 0) && ((reinterpret_cast<uintptr_t>(a.C) & 15) == 0);
+  const bool vec_out = ((a.ldc & 3) == 0) && ((reinterpret_cast<uintptr_t>(a.C) & 15) == 0);
   for (int64_t i = (int64_t)blockIdx.y * 4 + threadIdx.y; i < a.MF; i += (int64_t)gridDim.y * 4) {
     const int sa = (int)a.sftA[i] + gn.g;
     const int16_t* __restrict__ sB = a.sftB + (i / a.M) * a.N;
@@ -191,7 +191,7 @@ __global__ void __launch_bounds__(256) reconstruct_kernel(const ReconArgs a, con
           outv[e] = ldexp(v, sh);
         }
       }
-      double* crow = a.C + i * a.N;
+      double* crow = a.C + i * a.ldc;
       if (vec_out && j0 + 4 <= a.N) {
         *reinterpret_cast<double2*>(crow + j0) = make_double2(outv[0], outv[1]);
         *reinterpret_cast<double2*>(crow + j0 + 2) = make_double2(outv[2], outv[3]);
@@ -219,7 +219,7 @@ __global__ void __launch_bounds__(256, 2) reconstruct_fast_kernel(const ReconArg
   const int ng = (P + 6) / 7;
   const int64_t nq = (a.N + 3) >> 2;
   const int64_t plane = a.MF * a.ldn;
-  const bool vec_out = ((a.N & 3) == 0) && ((reinterpret_cast<uintptr_t>(a.C) & 15) == 0);
+  const bool vec_out = ((a.ldc & 3) == 0) && ((reinterpret_cast<uintptr_t>(a.C) & 15) == 0);
   for (int64_t i = (int64_t)blockIdx.y * 4 + threadIdx.y; i < a.MF; i += (int64_t)gridDim.y * 4) {
     const int sa = (int)a.sftA[i] + gn.g;
     const int16_t* __restrict__ sB = a.sftB + (a.M == a.MF ? 0 : (i / a.M) * a.N);
@@ -294,7 +294,7 @@ __global__ void __launch_bounds__(256, 2) reconstruct_fast_kernel(const ReconArg
           outv[e] = ldexp(v, sh);
         }
       }
-      double* crow = a.C + i * a.N;
+      double* crow = a.C + i * a.ldc;
       if (vec_out && j0 + 4 <= a.N) {
         *reinterpret_cast<double2*>(crow + j0) = make_double2(outv[0], outv[1]);
         *reinterpret_cast<double2*>(crow + j0 + 2) = make_double2(outv[2], outv[3]);

@@ -25,23 +25,26 @@ def emu():
 
 
 class chunk:
-    """Set F64E_PIPE_CHUNK for the duration of a block."""
+    """Set F64E_PIPE_CHUNK (and F64E_PIPE_COLS) for the duration of a block;
+    None leaves the library's default policy."""
 
-    def __init__(self, n):
-        self.n = n
+    def __init__(self, n, cols=None):
+        self.vals = {"F64E_PIPE_CHUNK": n, "F64E_PIPE_COLS": cols}
 
     def __enter__(self):
-        self.old = os.environ.get("F64E_PIPE_CHUNK")
-        if self.n is None:
-            os.environ.pop("F64E_PIPE_CHUNK", None)
-        else:
-            os.environ["F64E_PIPE_CHUNK"] = str(self.n)
+        self.old = {k: os.environ.get(k) for k in self.vals}
+        for k, v in self.vals.items():
+            if v is None:
+                os.environ.pop(k, None)
+            else:
+                os.environ[k] = str(v)
 
     def __exit__(self, *a):
-        if self.old is None:
-            os.environ.pop("F64E_PIPE_CHUNK", None)
-        else:
-            os.environ["F64E_PIPE_CHUNK"] = self.old
+        for k, v in self.old.items():
+            if v is None:
+                os.environ.pop(k, None)
+            else:
+                os.environ[k] = v
 
 
 def _pair(kind, batch, M, K, N, dist, seed):
@@ -55,8 +58,12 @@ def _pair(kind, batch, M, K, N, dist, seed):
 
 
 CASES = [
-    # (kind, batch, M, K, N, dist, chunk, kwargs)
+    # (kind, batch, M, K, N, dist, chunk or (chunk, column block), kwargs)
     ("mm_nt", 1, 1000, 700, 300, "randn", 384, {}),          # 3 chunks, the last ragged
+    ("mm_nt", 1, 1000, 700, 300, "randn", (384, 96), {}),    # + column blocks 96, 96, 96, 12 of row chunk 0
+    ("mm_nt", 1, 777, 513, 259, "wide16", (256, 64), {}),    # blocks widened to 80 (at most four)
+    ("mm", 1, 1030, 900, 520, "illcond40", (512, 256), {}),
+    ("mm", 1, 600, 1000, 200, "spike", (300, 48), {"nprimes": 13, "corr": False}),
     ("mm_nt", 1, 777, 513, 259, "wide16", 128, {}),          # 7 chunks of single-CTA GEMMs
     ("mm", 1, 1030, 900, 520, "illcond40", 512, {}),
     ("mm", 1, 600, 1000, 200, "spike", 256, {"nprimes": 13, "corr": False}),
@@ -72,12 +79,13 @@ CASES = [
 @pytest.mark.parametrize("case", CASES, ids=lambda c: f"{c[0]}-{c[1]}x{c[2]}x{c[3]}x{c[4]}-{c[5]}-c{c[6]}")
 def test_chunked_matches_unchunked_and_oracle(emu, oracle_mod, case):
     kind, batch, M, K, N, dist, per, kw = case
+    per, cols = per if isinstance(per, tuple) else (per, 0)
     A, B = _pair(kind, batch, M, K, N, dist, seed=M + K + N)
     fn = getattr(emu, kind)
     Ad, Bd = torch.from_numpy(A).cuda(), torch.from_numpy(B).cuda()
     with chunk(0):
         flat = fn(Ad, Bd, **kw)
-    with chunk(per):
+    with chunk(per, cols):
         chunked = fn(Ad, Bd, **kw)
     torch.cuda.synchronize()
     assert torch.equal(chunked, flat)
@@ -86,7 +94,7 @@ def test_chunked_matches_unchunked_and_oracle(emu, oracle_mod, case):
 
 
 @pytest.mark.parametrize("kind,shape", [("mm_nt", (4096, 2048, 1024)), ("mm", (2304, 1024, 2048)),
-                                        ("bmm_nt", (8, 256, 512, 384))])
+                                        ("mm_nt", (2048, 512, 4100)), ("bmm_nt", (8, 256, 512, 384))])
 def test_default_chunking_matches_unchunked(emu, kind, shape):
     # sizes where the default policy chunks (M >= 2048, or >= 4 members of >= 2048 rows in all)
     g = torch.Generator(device="cuda").manual_seed(sum(shape))
@@ -116,12 +124,16 @@ def test_gemm_events_count_chunk_launches(emu):
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(8)]
     for e in ev:
         e.record()
-    with chunk(256):
+    with chunk(256, 0):
         emu.ops.fp64_emu_gemm_ws(out, ws, A, Bt, pr, True, True, 53, True, 1, 0)
         n = emu.ops.fp64_emu_gemm_ws_ev(out, ws, A, Bt, pr, True, True, 53, True, 14, 0, [e.cuda_event for e in ev])
     torch.cuda.synchronize()
     assert n == 4
     assert all(ev[2 * i].elapsed_time(ev[2 * i + 1]) > 0 for i in range(4))
+    with chunk(256, 128):   # row chunk 0 in three column blocks: 3 + 3 GEMM launches
+        n = emu.ops.fp64_emu_gemm_ws_ev(out, ws, A, Bt, pr, True, True, 53, True, 14, 0, [e.cuda_event for e in ev])
+    torch.cuda.synchronize()
+    assert n == 6
     with chunk(0):
         assert torch.equal(out, emu.mm_nt(A, Bt))
     assert emu.ops.fp64_emu_status(ws) == 0
@@ -130,7 +142,7 @@ def test_gemm_events_count_chunk_launches(emu):
 def test_chunked_product_in_a_cuda_graph(emu):
     A = torch.randn(1100, 500, dtype=torch.float64, device="cuda")
     Bt = torch.randn(500, 260, dtype=torch.float64, device="cuda")
-    with chunk(300):
+    with chunk(300, 96):
         for _ in range(2):
             emu.mm_nt(A, Bt)                          # eager calls first: they create the library streams
         torch.cuda.synchronize()

@@ -505,6 +505,14 @@ void run_reconstruct(const Plan& l, const ModTables& T, const View& v, void* ws,
   launch_reconstruct(r, T, s);
 }
 
+// Device-to-host copy of one view's block of C (rows of pitch ldc) to the
+// same place in a host array shaped like C.
+cudaError_t copy_out(const View& v, const View& f, double* host, cudaStream_t s) {
+  double* dst = host + (v.C - f.C);
+  return cudaMemcpy2DAsync(dst, sizeof(double) * v.ldc, v.C, sizeof(double) * v.ldc, sizeof(double) * v.N,
+                           (size_t)(v.batch * v.M), cudaMemcpyDeviceToHost, s);
+}
+
 // ------------------------------------------------------------ pipelining --
 // A product whose three compute phases run in one call is cut into chunks.
 // A single product is cut into row blocks, and its first row block again
@@ -521,10 +529,10 @@ void run_reconstruct(const Plan& l, const ModTables& T, const View& v, void* ws,
 // the whole product.
 constexpr int kPipeMaxChunks = 16;
 constexpr int kPipeMaxCols = 4;
-constexpr int kPipeEvents = 4 * (kPipeMaxChunks + kPipeMaxCols) + 4;
+constexpr int kPipeEvents = 4 * (kPipeMaxChunks + kPipeMaxCols) + 8;
 
 struct PipeRes {
-  cudaStream_t hi[2] = {nullptr, nullptr}, aux = nullptr;
+  cudaStream_t hi[2] = {nullptr, nullptr}, aux = nullptr, cp = nullptr;   // cp: device-to-host copies
   cudaEvent_t ev[kPipeEvents] = {};
   std::mutex mtx;
 };
@@ -546,6 +554,7 @@ PipeRes* pipe_res(int dev, cudaStream_t s, int* rc) {
   PipeRes* r = new PipeRes;
   for (int i = 0; i < 2 && e == cudaSuccess; i++) e = cudaStreamCreateWithPriority(&r->hi[i], cudaStreamNonBlocking, hi);
   if (e == cudaSuccess) e = cudaStreamCreateWithPriority(&r->aux, cudaStreamNonBlocking, lo);
+  if (e == cudaSuccess) e = cudaStreamCreateWithPriority(&r->cp, cudaStreamNonBlocking, lo);
   for (int i = 0; i < kPipeEvents && e == cudaSuccess; i++) e = cudaEventCreateWithFlags(&r->ev[i], cudaEventDisableTiming);
   if (e != cudaSuccess) {
     *rc = cuda_fail(e, "pipeline streams");
@@ -606,7 +615,7 @@ Chunking pipe_chunking(const Plan& l) {
 }
 
 int run_pipelined(const Plan& l, const ModTables& T, const View& f, void* ws, const Dev& d, PipeRes* pr,
-                  const Chunking& ch, cudaStream_t s, void* const* gev, int ngev, int* launches) {
+                  const Chunking& ch, cudaStream_t s, void* const* gev, int ngev, int* launches, double* out_host) {
   const int64_t extent = ch.by_batch ? l.batch : l.M;
   const int C = (int)((extent + ch.per - 1) / ch.per);
   // GEMM units in launch order: the column blocks of row chunk 0, then row chunks 1.. (or member chunks).
@@ -672,11 +681,23 @@ int run_pipelined(const Plan& l, const ModTables& T, const View& f, void* ws, co
     if (2 * u + 1 < ngev) cudaEventRecord(static_cast<cudaEvent_t>(gev[2 * u + 1]), h);
     cudaEventRecord(E[e_gemm + u], h);
   }
+  const int e_done = e_gemm + U;
+  cudaError_t ec = cudaSuccess;
   for (int u = 0; u < U; u++) {
     cudaStreamWaitEvent(s, E[e_gemm + u], 0);   // joins both GEMM streams
     run_reconstruct(l, T, units[u], ws, l.recon_corr, units[u].corr, s);
+    if (out_host) {   // this block's copy to the host overlaps the later blocks' work
+      cudaEventRecord(E[e_done + u], s);
+      cudaStreamWaitEvent(pr->cp, E[e_done + u], 0);
+      if (ec == cudaSuccess) ec = copy_out(units[u], f, out_host, pr->cp);
+    }
+  }
+  if (out_host) {
+    cudaEventRecord(E[e_done + U], pr->cp);
+    cudaStreamWaitEvent(s, E[e_done + U], 0);   // joins the copy stream
   }
   e = cudaStreamWaitEvent(s, E[e_aux], 0);      // joins the extraction stream
+  if (e == cudaSuccess) e = ec;
   if (launches) *launches = U;
   if (rc) return rc;
   if (e == cudaSuccess) e = cudaGetLastError();
@@ -686,7 +707,7 @@ int run_pipelined(const Plan& l, const ModTables& T, const View& f, void* ws, co
 
 int run(const f64e_problem* p, const double* A, const double* B, double* out, void* ws, size_t ws_bytes,
         void* stream, int phases, bool checked, cudaEvent_t* ev, void* const* gev = nullptr, int ngev = 0,
-        int* launches = nullptr) {
+        int* launches = nullptr, double* out_host = nullptr) {
   if (launches) *launches = 0;
   Plan l;
   int rc = make_plan(p, &l);
@@ -696,7 +717,9 @@ int run(const f64e_problem* p, const double* A, const double* B, double* out, vo
   if (!A || !B || !out) return fail(F64E_ERR_ARGUMENT, "null operand pointer");
   if (l.K == 0) {
     if (phases & F64E_PHASE_COMPUTE) {
-      const cudaError_t e = cudaMemsetAsync(out, 0, sizeof(double) * l.MF * l.N, s);
+      cudaError_t e = cudaMemsetAsync(out, 0, sizeof(double) * l.MF * l.N, s);
+      if (e == cudaSuccess && out_host)
+        e = cudaMemcpyAsync(out_host, out, sizeof(double) * l.MF * l.N, cudaMemcpyDeviceToHost, s);
       if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync");
     }
     return F64E_OK;
@@ -723,7 +746,7 @@ int run(const f64e_problem* p, const double* A, const double* B, double* out, vo
     if (ch.per > 0) {
       PipeRes* pr = pipe_res(d.dev, s, &rc);
       if (rc) return rc;
-      if (pr) return run_pipelined(l, T, f, ws, d, pr, ch, s, gev, ngev, launches);
+      if (pr) return run_pipelined(l, T, f, ws, d, pr, ch, s, gev, ngev, launches, out_host);
     }
   }
   if (!l.deep) {
@@ -767,6 +790,10 @@ int run(const f64e_problem* p, const double* A, const double* B, double* out, vo
     run_reconstruct(l, T, f, ws, l.recon_corr, corr, s);
   }
   if (ev) cudaEventRecord(ev[4], s);
+  if (out_host && (phases & F64E_PHASE_RECON)) {
+    const cudaError_t e = copy_out(f, f, out_host, s);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpy2DAsync");
+  }
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "kernel launch");
   return F64E_OK;
@@ -836,6 +863,23 @@ int f64e_gemm_ev(const f64e_problem* p, const double* A, const double* B, double
   const int rc = run(p, A, B, out, ws, ws_bytes, stream, phases, false, nullptr, events, std::max(0, n_events), &nl);
   if (launches) *launches = nl;
   return rc;
+}
+
+int f64e_gemm_host(const f64e_problem* p, const double* A_host, const double* B_host, double* out_host,
+                   double* A_dev, double* B_dev, double* out_dev, void* ws, size_t ws_bytes, void* stream) {
+  g_err.clear();
+  Plan l;
+  int rc = make_plan(p, &l);
+  if (rc) return rc;
+  if (l.MF == 0 || l.NF == 0) return F64E_OK;
+  if (!A_host || !B_host || !out_host || !A_dev || !B_dev || !out_dev)
+    return fail(F64E_ERR_ARGUMENT, "null operand pointer");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaMemcpyAsync(A_dev, A_host, sizeof(double) * l.MF * l.K, cudaMemcpyHostToDevice, s);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(B_dev, B_host, sizeof(double) * l.NF * l.K, cudaMemcpyHostToDevice, s);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpyAsync");
+  return run(p, A_dev, B_dev, out_dev, ws, ws_bytes, stream, F64E_PHASE_ALL, false, nullptr, nullptr, 0, nullptr,
+             out_host);
 }
 
 int f64e_gemm_checked(const f64e_problem* p, const double* A, const double* B, double* out, void* ws,

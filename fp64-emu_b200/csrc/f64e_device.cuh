@@ -130,6 +130,10 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint64
   const uint64_t t0 = globaltimer_ns();
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
+    // Back off between polls: a warp spinning here would otherwise take issue
+    // slots from the kernels (extraction, reconstruction) that run beside the
+    // persistent GEMM on the same SM.
+    __nanosleep(128);
     if (globaltimer_ns() - t0 > limit_ns) {
       record_status(status, site);
       return false;

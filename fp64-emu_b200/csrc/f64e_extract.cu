@@ -296,7 +296,9 @@ __device__ __forceinline__ void cols_write_group(uint32_t (*sw)[kColTileN][kColP
   }
 }
 
-__global__ void __launch_bounds__(256) extract_cols_kernel(const ExtractArgs a, const ModTables T) {
+// Four blocks per SM (64 registers): the transposing kernel is latency-bound
+// and gains more from occupancy than it loses to the tighter register budget.
+__global__ void __launch_bounds__(256, 4) extract_cols_kernel(const ExtractArgs a, const ModTables T) {
   __shared__ uint32_t sw[kColGroup][kColTileN][kColPitch];
   const Gain gn = pick_gain(a.maxlg[0], a.maxlg[1], T.log2M, a.bits);
   const int be = gn.bits_eff;

@@ -21,6 +21,10 @@
 //   warps 2..5  epilogue: tcgen05.ld 32 lanes x 32 columns, Barrett, store.
 // Every mbarrier wait is bounded; a timeout records its site in the status
 // word and the CTA unwinds (draining its copies and MMAs, freeing TMEM).
+#include <map>
+#include <mutex>
+#include <set>
+
 #include "f64e_device.cuh"
 #include "f64e_kernels.h"
 
@@ -504,12 +508,19 @@ cudaError_t launch_residue_gemm(const CUtensorMap& tA, const CUtensorMap& tB, co
   const int ncs = g.corr_mode == 1 ? g.batch : (g.corr_mode == 2 ? 2 * g.batch : 0);
   const int64_t tiles = (int64_t)ntm * ntn * (g.P * g.batch + ncs);
   if (tiles <= 0) return cudaSuccess;
-  static bool attr_set = false;
-  if (!attr_set) {
-    const cudaError_t e =
-        cudaFuncSetAttribute(residue_gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES);
-    if (e != cudaSuccess) return e;
-    attr_set = true;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  {
+    // the shared-memory opt-in is a per-device attribute of the kernel
+    static std::mutex mtx;
+    static std::set<int> done;
+    std::lock_guard<std::mutex> lk(mtx);
+    if (!done.count(dev)) {
+      e = cudaFuncSetAttribute(residue_gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES);
+      if (e != cudaSuccess) return e;
+      done.insert(dev);
+    }
   }
   const int grid = (int)std::min<int64_t>(tiles, num_sms);
   residue_gemm_tc_kernel<<<grid, NUM_THREADS, SMEM_BYTES, s>>>(tA, tB, g, T);
@@ -520,10 +531,16 @@ cudaError_t launch_residue_gemm_pair(const CUtensorMap& tA, const CUtensorMap& t
                                      const ModTables& T, int num_sms, cudaStream_t s) {
   const int64_t tiles = total_tiles<PBM>(g);
   if (tiles <= 0) return cudaSuccess;
-  static int max_clusters = -1;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  // per device: the shared-memory opt-in and the resident cluster count
+  static std::mutex mtx;
+  static std::map<int, int> clusters_of;
+  std::unique_lock<std::mutex> lk(mtx);
+  int& max_clusters = clusters_of.emplace(dev, -1).first->second;
   if (max_clusters < 0) {
-    cudaError_t e =
-        cudaFuncSetAttribute(residue_gemm_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)PSMEM_BYTES);
+    e = cudaFuncSetAttribute(residue_gemm_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)PSMEM_BYTES);
     if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg = {};
     cudaLaunchAttribute attr[1];
@@ -542,6 +559,7 @@ cudaError_t launch_residue_gemm_pair(const CUtensorMap& tA, const CUtensorMap& t
     max_clusters = std::max(n, 1);
   }
   const int clusters = (int)std::min<int64_t>(tiles, max_clusters);
+  lk.unlock();
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;

@@ -245,6 +245,31 @@ int64_t gemm_ws_ev(at::Tensor& out, at::Tensor& ws, const at::Tensor& A, const a
   return launches;
 }
 
+// Host-resident product: A, B and out are CPU tensors (page-locked for the
+// copies to overlap); the device buffers and workspace come from torch's
+// caching allocator on the current device and stream.  The result blocks are
+// copied back while later blocks compute; the call returns once out holds
+// the product.
+void gemm_host(at::Tensor& out, const at::Tensor& A, const at::Tensor& B, const at::Tensor& primes_cpu, bool b_kn,
+               bool exact, int64_t bits, bool use_corr) {
+  TORCH_CHECK(!A.is_cuda() && !B.is_cuda() && !out.is_cuda(), "host product: A, B and out must be CPU tensors");
+  TORCH_CHECK(A.dtype() == at::kDouble && B.dtype() == at::kDouble && out.dtype() == at::kDouble, "f64 tensors");
+  TORCH_CHECK(A.is_contiguous() && B.is_contiguous() && out.is_contiguous(), "contig");
+  TORCH_CHECK(bits >= 16 && bits <= 53, "bits must be in [16, 53]");
+  const auto pr = host_primes(primes_cpu);
+  const f64e_problem p = problem_of(A, B, b_kn, pr, exact, bits, use_corr);
+  TORCH_CHECK(out.numel() == p.batch * p.M * p.N, "out f64 of batch*M*N");
+  const auto dev = at::TensorOptions().device(at::kCUDA, c10::cuda::current_device()).dtype(at::kDouble);
+  at::Tensor Ad = at::empty(A.sizes(), dev), Bd = at::empty(B.sizes(), dev), Cd = at::empty(out.sizes(), dev);
+  const size_t nb = f64e_workspace_size(&p);
+  TORCH_CHECK(nb > 0, "fp64_emu: ", f64e_last_error());
+  at::Tensor ws = at::empty({(int64_t)nb}, dev.dtype(at::kByte));
+  check(f64e_gemm_host(&p, A.data_ptr<double>(), B.data_ptr<double>(), out.data_ptr<double>(), Ad.data_ptr<double>(),
+                       Bd.data_ptr<double>(), Cd.data_ptr<double>(), ws.data_ptr(), nb, stream_of()));
+  const cudaError_t e = cudaStreamSynchronize(static_cast<cudaStream_t>(stream_of()));
+  TORCH_CHECK(e == cudaSuccess, "fp64_emu: ", cudaGetErrorString(e));
+}
+
 void gemm_checked(at::Tensor& out, at::Tensor& ws, const at::Tensor& A, const at::Tensor& B,
                   const at::Tensor& primes_cpu, bool b_kn, bool exact, int64_t bits, bool use_corr) {
   gemm_phase(out, ws, A, B, primes_cpu, b_kn, exact, bits, use_corr, F64E_PHASE_ALL, true, 0);
@@ -301,6 +326,9 @@ TORCH_LIBRARY(fp64_emu_b200, ops) {
       "fp64_emu_gemm_ws_ev(Tensor! out, Tensor! ws, Tensor A, Tensor B, Tensor primes_cpu, bool b_kn, bool exact, "
       "int bits, bool use_corr, int phases, int slab_cols, int[] events) -> int");
   ops.def(
+      "fp64_emu_gemm_host(Tensor! out, Tensor A, Tensor B, Tensor primes_cpu, bool b_kn, bool exact, int bits, "
+      "bool use_corr) -> ()");
+  ops.def(
       "fp64_emu_gemm_checked(Tensor! out, Tensor! ws, Tensor A, Tensor B, Tensor primes_cpu, bool b_kn, bool "
       "exact, int bits, bool use_corr) -> ()");
   ops.def("fp64_emu_status(Tensor ws) -> int");
@@ -312,6 +340,9 @@ TORCH_LIBRARY(fp64_emu_b200, ops) {
   ops.impl("fp64_emu_workspace_bytes", &workspace_bytes);
   ops.impl("fp64_emu_set_wait_limit_ns", &set_wait_limit_ns);
 }
+
+// The host product's tensors live on the CPU; its work runs on the current CUDA device.
+TORCH_LIBRARY_IMPL(fp64_emu_b200, CPU, ops) { ops.impl("fp64_emu_gemm_host", &gemm_host); }
 
 TORCH_LIBRARY_IMPL(fp64_emu_b200, CUDA, ops) {
   ops.impl("fp64_emu_mm", &mm);

@@ -145,6 +145,50 @@ def mm_timed(A: torch.Tensor, B: torch.Tensor, nprimes: int = None, exact: bool 
     return out, times.tolist()
 
 
+def _host_product(A, B, b_kn, out, nprimes, exact, bits, corr):
+    assert A.dim() == B.dim() and A.dim() in (2, 3)
+    K = A.size(-1)
+    if A.dim() == 3:
+        shape = (A.size(0), A.size(1), B.size(2) if b_kn else B.size(1))
+    else:
+        shape = (A.size(0), B.size(1) if b_kn else B.size(0))
+    nprimes, corr = _defaults(K, nprimes, corr)
+    primes = _tables(nprimes)[0]
+    if out is None:
+        out = torch.empty(shape, dtype=torch.float64, pin_memory=A.is_pinned())
+    Ac = A if A.is_contiguous() else A.contiguous()
+    Bc = B if B.is_contiguous() else B.contiguous()
+    ops.fp64_emu_gemm_host(out, Ac, Bc, primes, b_kn, exact, bits, corr)
+    return out
+
+
+def mm_nt_host(A: torch.Tensor, Bt: torch.Tensor, out: torch.Tensor = None, nprimes: int = None,
+               exact: bool = True, bits: int = 53, corr: bool = None) -> torch.Tensor:
+    """mm_nt for operands and result in host memory, on the current CUDA
+    device: the operands are copied in, and each finished block of C is copied
+    back while later blocks are still computing.  Use page-locked tensors
+    (pin_memory) for the copies to overlap.  Returns once `out` holds C."""
+    return _host_product(A, Bt, True, out, nprimes, exact, bits, corr)
+
+
+def mm_host(A: torch.Tensor, B: torch.Tensor, out: torch.Tensor = None, nprimes: int = None,
+            exact: bool = True, bits: int = 53, corr: bool = None) -> torch.Tensor:
+    """mm (B given as [N, K]) for host-resident operands; see mm_nt_host."""
+    return _host_product(A, B, False, out, nprimes, exact, bits, corr)
+
+
+def bmm_nt_host(A: torch.Tensor, Bt: torch.Tensor, out: torch.Tensor = None, nprimes: int = None,
+                exact: bool = True, bits: int = 53, corr: bool = None) -> torch.Tensor:
+    """bmm_nt for host-resident operands; see mm_nt_host."""
+    return _host_product(A, Bt, True, out, nprimes, exact, bits, corr)
+
+
+def bmm_host(A: torch.Tensor, B: torch.Tensor, out: torch.Tensor = None, nprimes: int = None,
+             exact: bool = True, bits: int = 53, corr: bool = None) -> torch.Tensor:
+    """bmm for host-resident operands; see mm_nt_host."""
+    return _host_product(A, B, False, out, nprimes, exact, bits, corr)
+
+
 def range_bits(nprimes: int) -> float:
     """Signed CRT range of the first `nprimes` moduli, in bits."""
     r = 0.0
@@ -173,4 +217,7 @@ def plan(K: int, bits: int = 53) -> int:
     raise ValueError(f"K={K} at bits={bits} needs more range than {_MAXP} primes give")
 
 
-__all__ = ["mm", "mm_nt", "bmm", "bmm_nt", "mm_timed", "plan", "plan_config", "range_bits"]
+from .host import HostStream  # noqa: E402  (uses _defaults and _tables above)
+
+__all__ = ["mm", "mm_nt", "bmm", "bmm_nt", "mm_timed", "plan", "plan_config", "range_bits",
+           "mm_host", "mm_nt_host", "bmm_host", "bmm_nt_host", "HostStream"]

@@ -2,8 +2,8 @@
 NCCL for the plumbing.
 
 The product shards with no data-path collective:
-  * mm / mm_nt: C is split into a pr x pc grid of blocks (2-D: 2 -> 2x1,
-    4 -> 2x2, 8 -> 4x2); rank (i, j) holds A's row block i and B's column
+  * mm / mm_nt: C is split into a pr x pc grid of blocks (2-D: 2 -> 1x2,
+    4 -> 2x2, 8 -> 2x4); rank (i, j) holds A's row block i and B's column
     block j, so each rank extracts only its own share of both operands;
   * bmm / bmm_nt: the batch is split.
 The only collective on the timed path is one MAX all-reduce of two floats
@@ -25,11 +25,16 @@ PHASE_COMPUTE = PHASE_EXTRACT | PHASE_GEMM | PHASE_RECON
 
 
 def grid_shape(world):
-    """(row blocks, column blocks) of the 2-D partition for `world` ranks."""
-    pc = 1
-    while (pc * 2) ** 2 <= world and world % (pc * 2) == 0:
-        pc *= 2
-    return world // pc, pc
+    """(row blocks, column blocks) of the 2-D partition for `world` ranks: as
+    square as the rank count allows, with the extra factor on the columns
+    (2 -> 1x2, 4 -> 2x2, 8 -> 2x4).  Each rank extracts its rows of A and its
+    columns of B; the rows of A are extracted chunk by chunk behind the GEMM,
+    while B's columns are extracted before it starts, so B is the operand to
+    split further."""
+    pr = 1
+    while (pr * 2) ** 2 <= world and world % (pr * 2) == 0:
+        pr *= 2
+    return pr, world // pr
 
 
 def block_range(n, parts, i):

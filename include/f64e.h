@@ -163,6 +163,18 @@ F64E_API void f64e_set_wait_limit_ns(uint64_t ns);
 /* Message of the last failed call on this thread ("" if none). */
 F64E_API const char* f64e_last_error(void);
 
+/* The whole product with operands and result in host memory: copies A and B
+ * into the caller's device buffers (A_dev: batch*M*K doubles, B_dev:
+ * batch*N*K, out_dev: batch*M*N), runs every phase, and copies each finished
+ * block of the result back to out_host while later blocks are still being
+ * computed, all on `stream`.  Host buffers should be page-locked for the
+ * copies to overlap the computation; the result is in out_host once the
+ * stream reaches this call's end.  No reference counterpart (the reference's
+ * ops take device tensors; a caller there copies around the call). */
+F64E_API int f64e_gemm_host(const f64e_problem* p, const double* A_host, const double* B_host, double* out_host,
+                   double* A_dev, double* B_dev, double* out_dev, void* workspace, size_t workspace_bytes,
+                   void* stream);
+
 /* Self-check aid: the same product as f64e_gemm with the modular GEMM done by
  * a plain dp4a kernel instead of the tensor-core kernel (slow; for tests). */
 F64E_API int f64e_gemm_checked(const f64e_problem* p, const double* A, const double* B, double* out,

@@ -116,7 +116,7 @@ def test_local_sizing_alone_can_differ():
 def test_grid_shapes():
     from fp64_emu import dist as proto_mod
     proto = vars(proto_mod)
-    assert [proto["grid_shape"](w) for w in (1, 2, 4, 8)] == [(1, 1), (2, 1), (2, 2), (4, 2)]
+    assert [proto["grid_shape"](w) for w in (1, 2, 4, 8)] == [(1, 1), (1, 2), (2, 2), (2, 4)]
     blocks = [proto["rank_block"](r, 8, 8192, 8192) for r in range(8)]
     cover = np.zeros((8, 8), dtype=int)
     for (r0, r1), (c0, c1) in blocks:

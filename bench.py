@@ -319,6 +319,13 @@ def run_ours(args):
         part = f"2-D C blocks {pr}x{pc}"
     A_host_full = A.cpu() if (rank == 0 and world == 1 and not args.no_cpu) else None
     B_host_full = B.cpu() if (rank == 0 and world == 1 and not args.no_cpu) else None
+    shs = shares = None
+    if world > 1 and batch == 1:
+        # e2e at N > 1: every rank copies in a disjoint share of its blocks and
+        # the blocks are completed over NVLink (fp64_emu.dist.ShardedHostStream)
+        from fp64_emu.dist import ShardedHostStream
+        shs = ShardedHostStream(kind, M, N, K, nprimes=nprimes, corr=corr)
+        shares = shs.host_shares(A.cpu(), B.cpu())
     del A, B
     torch.cuda.empty_cache()
 
@@ -347,15 +354,19 @@ def run_ours(args):
 
     # e2e through the public API with host buffers.
     import fp64_emu
-    A_pin = A_l.cpu().pin_memory()
-    B_pin = B_l.cpu().pin_memory()
-    out_pin = torch.empty(step.out.shape, dtype=torch.float64).pin_memory()
-    A_d = torch.empty_like(A_l)
-    B_d = torch.empty_like(B_l)
+    if shs is None:
+        A_pin = A_l.cpu().pin_memory()
+        B_pin = B_l.cpu().pin_memory()
+        out_pin = torch.empty(step.out.shape, dtype=torch.float64).pin_memory()
+        A_d = torch.empty_like(A_l)
+        B_d = torch.empty_like(B_l)
 
     hs = fp64_emu.HostStream(kind, nprimes=nprimes, corr=corr) if world == 1 else None
 
     def e2e_step():
+        if shs is not None:
+            shs.submit(*shares)
+            return
         if hs is not None:
             # a stream of host-resident products: the operand copies, the
             # product and the result copy of neighbouring steps overlap
@@ -371,8 +382,9 @@ def run_ours(args):
     e2e_steps = max(3, min(args.steps, 20))
     for _ in range(2):
         e2e_step()
-    if hs is not None:
-        hs.synchronize()
+    for x in (hs, shs):
+        if x is not None:
+            x.synchronize()
     torch.cuda.synchronize()
     barrier()
     e0 = torch.cuda.Event(enable_timing=True)
@@ -380,8 +392,9 @@ def run_ours(args):
     e0.record()
     for _ in range(e2e_steps):
         e2e_step()
-    if hs is not None:
-        hs.join()   # the current stream waits for every step's result copy
+    for x in (hs, shs):
+        if x is not None:
+            x.join()   # the current stream waits for every step's result copy
     e1.record()
     torch.cuda.synchronize()
     barrier()
@@ -391,8 +404,11 @@ def run_ours(args):
     ms = max_over_ranks(ms_local)
     gemm_ms = max_over_ranks(gemm_ms_local)
     e2e_ms = max_over_ranks(e2e_ms_local)
-    h2d = (A_l.numel() + B_l.numel()) * 8
-    d2h = step.out.numel() * 8
+    # whole job, summed over ranks: the shares copied in, the blocks copied out
+    if shs is not None:
+        h2d, d2h = (M * K + K * N) * 8, M * N * 8
+    else:
+        h2d, d2h = (A_l.numel() + B_l.numel()) * 8 * world, step.out.numel() * 8 * world
 
     # Roofline of the dominant kernel on this rank.
     G = nprimes + (2 if corr else 0)
@@ -429,8 +445,10 @@ def run_ours(args):
                    "compute": "s8 x s8 -> s32 tcgen05 residue GEMMs, exact int128 recombine"},
         "e2e": {"value": round(work / (e2e_ms * 1e-3) / 1e12, 3), "unit": UNIT, "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h,
-                "api": "fp64_emu.HostStream (operand copies, product and result copy of neighbouring steps "
-                       "overlap)" if world == 1 else "fp64_emu.dist.ShardedProduct with explicit copies"},
+                "api": ("fp64_emu.HostStream (operand copies, product and result copy of neighbouring steps "
+                        "overlap)") if world == 1 else
+                       ("fp64_emu.dist.ShardedHostStream (disjoint host shares, NVLink all-gathers, overlapped "
+                        "stages)" if shs is not None else "fp64_emu.dist.ShardedProduct with explicit copies")},
         "gpu_launches": sum(our_kernel_launches_per_step(kind, A_l.shape[0] if A_l.dim() == 3 else 1, c)
                             for c in launches),
         "roofline": {"bound": "tensor", "kernel": "residue_gemm_pair_kernel" if Ml > 128 else "residue_gemm_tc_kernel",

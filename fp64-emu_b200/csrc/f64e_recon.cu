@@ -55,15 +55,19 @@ __device__ __forceinline__ I128 i128_mul_add(I128 a, uint64_t m, int64_t d) {
   return r;
 }
 
-// a * m + d for signed 64-bit a, 0 < m < 2^63, signed d: the sign of a
-// contributes -m to the high word instead of a full second product.
+// a * m + d for signed 64-bit a, 0 < m < 2^63, signed d: the unsigned
+// product of a's bit pattern from four 32 x 32 -> 64 partial products, then
+// -m * 2^64 when a < 0.
 __device__ __forceinline__ I128 i128_mul_add_s64(int64_t a, uint64_t m, int64_t d) {
   const uint64_t au = (uint64_t)a;
-  const uint64_t lo = au * m;
-  uint64_t hi = __umul64hi(au, m) - (a < 0 ? m : 0ULL);
+  const uint32_t al = (uint32_t)au, ah = (uint32_t)(au >> 32), ml = (uint32_t)m, mh = (uint32_t)(m >> 32);
+  const uint64_t p00 = (uint64_t)al * ml, p01 = (uint64_t)al * mh, p10 = (uint64_t)ah * ml, p11 = (uint64_t)ah * mh;
+  const uint64_t mid = (p00 >> 32) + (uint32_t)p01 + (uint32_t)p10;
+  const uint64_t lo = (mid << 32) | (uint32_t)p00;
+  const uint64_t hi = p11 + (p01 >> 32) + (p10 >> 32) + (mid >> 32) - (a < 0 ? m : 0ULL);
   I128 r;
   r.lo = lo + (uint64_t)d;
-  r.hi = (int64_t)(hi + (r.lo < lo ? 1ULL : 0ULL) + (d < 0 ? ~0ULL : 0ULL));
+  r.hi = (int64_t)(hi + (r.lo < lo ? 1ULL : 0ULL) + (uint64_t)(d >> 63));
   return r;
 }
 
@@ -96,6 +100,27 @@ __device__ __forceinline__ double i128_to_double(I128 v) {
     m = scale2(__ull2double_rn(top | (tail ? 1ULL : 0ULL)), sh);
   }
   return neg ? -m : m;
+}
+
+// RNE(v) * 2^e in one step: the top 64 significant bits with the dropped
+// tail folded into a sticky bit convert with one rounding; the power of two
+// of that conversion and e are applied together (exact for normal results,
+// ldexp's rounding otherwise).
+__device__ __forceinline__ double i128_to_double_scaled(I128 v, int e) {
+  const uint64_t sg = (uint64_t)(v.hi >> 63);
+  uint64_t lo = v.lo ^ sg, hi = (uint64_t)v.hi ^ sg;
+  lo -= sg;                                  // two's complement magnitude: + 1 when negative
+  hi += (sg & (lo == 0ULL ? 1ULL : 0ULL));
+  uint64_t top = lo;
+  int sh = 0;
+  if (hi != 0) {
+    const int lz = __clzll((long long)hi);  // 0..63
+    sh = 64 - lz;
+    top = lz ? ((hi << lz) | (lo >> sh)) : hi;
+    top |= ((lz ? (lo << lz) : lo) != 0ULL) ? 1ULL : 0ULL;
+  }
+  const double m = __ull2double_rn(top);
+  return scale2(sg ? -m : m, sh + e);
 }
 
 template <int CM>
@@ -285,7 +310,7 @@ __global__ void __launch_bounds__(256, 2) reconstruct_fast_kernel(const ReconArg
             v = i128_of(a0);
           }
           if (CM != 0) v = i128_add_shl(v, cr[e], cshift);
-          outv[e] = scale2(i128_to_double(v), sh);
+          outv[e] = i128_to_double_scaled(v, sh);
         } else {
           double v = (double)((ng == 3) ? a2 : ((ng == 2) ? a1 : a0));
           if (ng == 3) v = fma(v, (double)T.m64[1], (double)a1);

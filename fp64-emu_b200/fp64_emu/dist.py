@@ -114,3 +114,143 @@ def bmm_nt_sharded(A_b, Bt_b, batch_total, group=None, **kw):
     """This rank's members C[b] = A[b] @ Bt[b] of a batch of batch_total."""
     out = torch.empty(A_b.size(0), A_b.size(1), Bt_b.size(2), dtype=torch.float64, device=A_b.device)
     return ShardedProduct(A_b, Bt_b, True, batch_total * Bt_b.size(2), A_b.size(2), group=group, **kw).run(out)
+
+
+class ShardedHostStream:
+    """A stream of partitioned products whose operands and results live in host
+    memory, one process per GPU.
+
+    Rank (i, j) of the pr x pc grid owns C's block (i, j) and needs A's row
+    block i and B's column block j.  Over PCIe each rank copies in only a
+    disjoint share of those blocks (A's row block split over the pc ranks of
+    grid row i, B's column block split over the pr ranks of grid column j), so
+    the whole job moves each operand byte across PCIe once, as on one GPU; two
+    NCCL all-gathers over NVLink (within the grid row and within the grid
+    column) complete the blocks on the device.  Then the usual sizing
+    (+ MAX all-reduce) and product, and the copy of the rank's C block back.
+    With `depth` buffer sets in rotation on four streams (copy in, gather,
+    compute, copy out), neighbouring products overlap stage by stage.
+
+    Host layout: `host_shares(A, B)` cuts a full host A and B into this rank's
+    shares (once, outside any timed loop); submit(a_share, b_share, c_block)
+    takes page-locked CPU tensors shaped like those shares and this rank's C
+    block.  kind: "mm_nt" (B given as [K, N]) or "mm" (B as [N, K])."""
+
+    def __init__(self, kind, M, N, K, nprimes=None, exact=True, bits=53, corr=None, depth=2):
+        if kind not in ("mm", "mm_nt"):
+            raise ValueError("kind must be mm or mm_nt")
+        self.kind, self.b_kn = kind, kind == "mm_nt"
+        self.M, self.N, self.K = M, N, K
+        self.world, self.rank = dist.get_world_size(), dist.get_rank()
+        self.pr, self.pc = grid_shape(self.world)
+        self.gi, self.gj = divmod(self.rank, self.pc)
+        (self.r0, self.r1), (self.c0, self.c1) = rank_block(self.rank, self.world, M, N)
+        self.mb, self.nb = self.r1 - self.r0, self.c1 - self.c0
+        # every rank creates every row and column group, in the same order
+        self.row_groups = [dist.new_group([i * self.pc + j for j in range(self.pc)]) for i in range(self.pr)]
+        self.col_groups = [dist.new_group([i * self.pc + j for i in range(self.pr)]) for j in range(self.pc)]
+        self.row_group, self.col_group = self.row_groups[self.gi], self.col_groups[self.gj]
+        # shares: A rows of the row block over the pc ranks of the grid row;
+        # B's block (as [K, nb] or [nb, K]) split along its first dimension
+        # over the pr ranks of the grid column; padded to equal sizes for the
+        # all-gathers
+        self.a_rows = -(-self.mb // self.pc)
+        self.b_rows = -(-(K if self.b_kn else self.nb) // self.pr)
+        self.nprimes, self.exact, self.bits, self.corr = nprimes, exact, bits, corr
+        self.depth = max(1, int(depth))
+        dev = torch.device("cuda", torch.cuda.current_device())
+        self.dev = dev
+        self.streams = [torch.cuda.Stream(dev) for _ in range(4)]
+        self.slots = [None] * self.depth
+        self.n = 0
+
+    def a_share_range(self):
+        """Rows of A (global indices) this rank copies in."""
+        a0 = min(self.mb, self.gj * self.a_rows)
+        return self.r0 + a0, self.r0 + min(self.mb, a0 + self.a_rows)
+
+    def b_share_range(self):
+        """First-dimension range of B's column block ([K, nb] or [nb, K]) this rank copies in."""
+        ext = self.K if self.b_kn else self.nb
+        b0 = min(ext, self.gi * self.b_rows)
+        return b0, min(ext, b0 + self.b_rows)
+
+    def host_shares(self, A, B):
+        """This rank's page-locked shares of full host operands A [M, K] and
+        B ([K, N] or [N, K]), and a page-locked C block to receive results."""
+        a0, a1 = self.a_share_range()
+        b0, b1 = self.b_share_range()
+        blk = B[:, self.c0:self.c1] if self.b_kn else B[self.c0:self.c1]
+        a = A[a0:a1].contiguous().pin_memory()
+        b = blk[b0:b1].contiguous().pin_memory()
+        c = torch.empty(self.mb, self.nb, dtype=torch.float64).pin_memory()
+        return a, b, c
+
+    def _slot(self, k):
+        s = self.slots[k]
+        if s is not None:
+            return s
+        dev, K = self.dev, self.K
+        bshape_full = (K, self.nb) if self.b_kn else (self.nb, K)
+        with torch.cuda.stream(self.streams[2]):
+            s = {"a_sh": torch.empty(self.a_rows, K, dtype=torch.float64, device=dev),
+                 "b_sh": torch.empty((self.b_rows,) + bshape_full[1:], dtype=torch.float64, device=dev),
+                 "a_all": torch.empty(self.pc * self.a_rows, K, dtype=torch.float64, device=dev),
+                 "b_all": torch.empty((self.pr * self.b_rows,) + bshape_full[1:], dtype=torch.float64, device=dev),
+                 "C": torch.empty(self.mb, self.nb, dtype=torch.float64, device=dev)}
+            s["A"] = s["a_all"][:self.mb]
+            s["B"] = s["b_all"][:bshape_full[0]]
+            s["sp"] = ShardedProduct(s["A"], s["B"], self.b_kn, self.N, K, nprimes=self.nprimes, exact=self.exact,
+                                     bits=self.bits, corr=self.corr)
+        for name in ("loaded", "gathered", "computed", "done"):
+            s[name] = torch.cuda.Event()
+        s["used"] = False
+        self.slots[k] = s
+        return s
+
+    def submit(self, a_share, b_share, c_block):
+        """Queue this rank's part of one product; every rank calls submit in
+        the same order.  Returns at once; c_block holds the rank's C block
+        after synchronize()."""
+        h2d, comm, comp, d2h = self.streams
+        s = self._slot(self.n % self.depth)
+        cur = torch.cuda.current_stream(self.dev)
+        for st in self.streams:
+            st.wait_stream(cur)
+        if s["used"]:
+            h2d.wait_event(s["gathered"])    # the share buffers were gathered from
+            comm.wait_event(s["computed"])   # the blocks were read by the product
+            comp.wait_event(s["done"])       # the C block left the device
+        with torch.cuda.stream(h2d):
+            s["a_sh"][:a_share.size(0)].copy_(a_share, non_blocking=True)
+            s["b_sh"][:b_share.size(0)].copy_(b_share, non_blocking=True)
+            s["loaded"].record(h2d)
+        comm.wait_event(s["loaded"])
+        with torch.cuda.stream(comm):
+            dist.all_gather_into_tensor(s["a_all"], s["a_sh"], group=self.row_group)
+            dist.all_gather_into_tensor(s["b_all"], s["b_sh"], group=self.col_group)
+            s["gathered"].record(comm)
+        comp.wait_event(s["gathered"])
+        with torch.cuda.stream(comp):
+            sp = s["sp"]
+            sp.sizing(s["C"])
+            sp._phase(s["C"], PHASE_COMPUTE)
+            s["computed"].record(comp)
+        d2h.wait_event(s["computed"])
+        with torch.cuda.stream(d2h):
+            c_block.copy_(s["C"], non_blocking=True)
+            s["done"].record(d2h)
+        s["used"] = True
+        self.n += 1
+        return c_block
+
+    def join(self, stream=None):
+        st = stream or torch.cuda.current_stream(self.dev)
+        for s in self.slots:
+            if s is not None and s["used"]:
+                st.wait_event(s["done"])
+
+    def synchronize(self):
+        for s in self.slots:
+            if s is not None and s["used"]:
+                s["done"].synchronize()

@@ -88,3 +88,56 @@ def test_partitioned_matches_single_gpu(case, tmp_path):
         for r in range(world):
             (r0, r1), (c0, c1) = rank_block(r, world, M, N)
             assert torch.equal(blocks[r], full[r0:r1, c0:c1])
+
+
+def _host_worker(rank, world, port, case, outdir):
+    for p in (ROOT, os.path.join(ROOT, "fp64-emu_b200")):
+        if p not in sys.path:
+            sys.path.insert(0, p)
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    import torch.distributed as dist
+    from datetime import timedelta
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=120),
+                            device_id=torch.device("cuda", rank))
+    try:
+        from fp64_emu.dist import ShardedHostStream
+        kind, M, K, N = case
+        g = torch.Generator().manual_seed(321)
+        outs = []
+        hs = ShardedHostStream(kind, M, N, K, depth=2)
+        for step in range(3):   # three products through the rotating buffers
+            A = torch.randn(M, K, dtype=torch.float64, generator=g)
+            B = torch.randn((K, N) if kind == "mm_nt" else (N, K), dtype=torch.float64, generator=g) * 2.0 ** step
+            A[M // 2:] = 1.0
+            a, b, c = hs.host_shares(A, B)
+            hs.submit(a, b, c)
+            outs.append(c)
+        hs.synchronize()
+        torch.save([o.clone() for o in outs], os.path.join(outdir, f"hblock{rank}.pt"))
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("case", [("mm_nt", 700, 1500, 900), ("mm", 520, 640, 333)])
+def test_sharded_host_stream_matches_single_gpu(case, tmp_path):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import torch.multiprocessing as mp
+    world = 2
+    mp.start_processes(_host_worker, args=(world, _port(), case, str(tmp_path)), nprocs=world, join=True,
+                       start_method="spawn")
+    import fp64_emu
+    from fp64_emu.dist import rank_block
+    kind, M, K, N = case
+    g = torch.Generator().manual_seed(321)
+    blocks = [torch.load(tmp_path / f"hblock{r}.pt") for r in range(world)]
+    for step in range(3):
+        A = torch.randn(M, K, dtype=torch.float64, generator=g)
+        B = torch.randn((K, N) if kind == "mm_nt" else (N, K), dtype=torch.float64, generator=g) * 2.0 ** step
+        A[M // 2:] = 1.0
+        full = getattr(fp64_emu, kind)(A.cuda(), B.cuda()).cpu()
+        for r in range(world):
+            (r0, r1), (c0, c1) = rank_block(r, world, M, N)
+            assert torch.equal(blocks[r][step], full[r0:r1, c0:c1])

@@ -312,17 +312,25 @@ __global__ void __launch_bounds__(256, 4) extract_cols_kernel(const ExtractArgs 
   const bool col_fast = (s >= -960) && (s <= 960);
   const double p2s = pow2d(col_fast ? s : 0), p2h = pow2d(7 - be);
   const double* __restrict__ xb = a.X + b * a.K * a.ld + n;   // row pitch a.ld (>= a.N)
+  // all eight loads first (the out-of-line slow split would otherwise hold
+  // the second quad's loads back until the first quad is split)
+  double x[2][4];
+#pragma unroll
+  for (int qi = 0; qi < 2; qi++)
+#pragma unroll
+    for (int u = 0; u < 4; u++) {
+      const int64_t k = k0 + 4 * (ty + 8 * qi) + u;
+      x[qi][u] = (nin && k < a.K) ? __ldg(xb + k * a.ld) : 0.0;
+    }
   Split S[2][4];
   bool ok[2];
 #pragma unroll
   for (int qi = 0; qi < 2; qi++) {
-    const int64_t kb = k0 + 4 * (ty + 8 * qi);
     ok[qi] = true;
 #pragma unroll
     for (int u = 0; u < 4; u++) {
-      const int64_t k = kb + u;
-      const double x = (nin && k < a.K) ? __ldg(xb + k * a.ld) : 0.0;
-      if (!(col_fast && split_fast(x, p2s, p2h, be, corr, S[qi][u]))) S[qi][u] = split_slow(x, s, be, corr);
+      if (!(col_fast && split_fast(x[qi][u], p2s, p2h, be, corr, S[qi][u])))
+        S[qi][u] = split_slow(x[qi][u], s, be, corr);
       ok[qi] = ok[qi] && (S[qi][u].u >> 56) == 0;
     }
   }

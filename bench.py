@@ -153,12 +153,13 @@ def int8_peak_from_file():
         return 2.0 * 1400.0, 2.0 * 1590.0, "fallback"
 
 
-def profiled_traffic_per_launch():
-    """dram bytes (read + write) per GEMM launch from the committed ncu summary."""
+def profiled_traffic_per_step():
+    """DRAM bytes (read + write) of all GEMM launches of one C2 step (the
+    chunked pipeline's GEMM chunks) from the committed ncu summary."""
     try:
         with open(PROFILE_SUMMARY) as f:
             for line in f:
-                if line.strip().startswith("dram_bytes_per_launch"):
+                if line.strip().startswith("dram_bytes_per_step"):
                     return int(float(line.split("=")[1].split()[0]))
     except (OSError, ValueError, IndexError):
         pass
@@ -424,7 +425,7 @@ def run_ours(args):
     peak = peak_burst if held else peak_sus
     mhz = (clk or {}).get("sm_mhz") or 1965.0
     nominal = 148 * 8192 * 2 * mhz * 1e6 / 1e12   # 8192 INT8 MAC/clk/SM at the sampled clock
-    traffic = profiled_traffic_per_launch() if (args.workload == "C2" and world == 1) else None
+    traffic = profiled_traffic_per_step() if (args.workload == "C2" and world == 1) else None
 
     result = {
         "metric": METRIC if args.workload == "C2" else f"emulated FP64 TFLOP/s (2MNK/t), {args.workload}",
@@ -458,7 +459,8 @@ def run_ours(args):
                                   f"{'burst: SM clock held' if held else 'sustained: SM clock sagged'}); "
                                   f"nominal 8192 MAC/clk/SM at the sampled clock = {nominal:.0f} TOPS, "
                                   f"frac of nominal {achieved / nominal:.3f}",
-                     "gemm_ms_per_step": round(gemm_ms, 4), "traffic": traffic},
+                     "gemm_ms_per_step": round(gemm_ms, 4), "traffic": traffic,
+                     "per": "step: achieved over the step's GEMM busy time, traffic summed over its GEMM launches"},
         "phases_ms": {"gemm_busy": round(gemm_ms, 4), "outside_gemm": round(ms - gemm_ms, 4),
                       "gemm_launches_per_step": launches[-1] if launches else 0},
         "clocks": clk,

@@ -236,12 +236,15 @@ def max_over_ranks(x):
 
 
 def our_kernel_launches_per_step(kind, batch, chunks):
-    # sizing: row stats of A + (column partial + finalize, or row stats) of B
-    # + operand maxima; per chunk one extraction of A, one GEMM and one
+    # sizing: row stats of A + column partials + column finalize with the
+    # operand maxima (B as [K, N]), or one launch for both operands' row stats
+    # and the maxima; per chunk one extraction of A, one GEMM and one
     # reconstruction; B extracted once (single product) or per chunk (batch).
+    # (Products small enough to extract both operands in one launch do not
+    # occur in the bench's workloads.)
     nt = kind in ("mm_nt", "bmm_nt")
     c = max(1, chunks)
-    return (1 + (2 if nt else 1) + 1) + 3 * c + (1 if batch == 1 else c)
+    return (3 if nt else 1) + 3 * c + (1 if batch == 1 else c)
 
 
 def cpu_baseline_oracle(A_cpu, Bt_cpu, nprimes, corr, rows):

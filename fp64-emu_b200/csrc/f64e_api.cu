@@ -284,15 +284,18 @@ T* at(void* ws, size_t off) {
 
 int run_sizing(const Plan& l, const double* A, const double* B, void* ws, cudaStream_t s) {
   WsHead* head = at<WsHead>(ws, 0);
-  cudaError_t e = cudaMemsetAsync(&head->status, 0, sizeof(int32_t), s);
+  // status word and the CTA counter of the launch that takes the operand maxima
+  cudaError_t e = cudaMemsetAsync(&head->status, 0, 2 * sizeof(int32_t), s);
   if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync");
-  launch_row_stats(A, l.MF, l.K, l.bits, at<int16_t>(ws, l.o_sftA), at<float>(ws, l.o_lgA), s);
-  if (l.nt)
-    launch_col_stats(B, l.batch, l.K, l.N, l.kslab, l.nslab, l.bits, at<int16_t>(ws, l.o_sftB),
-                     at<float>(ws, l.o_lgB), at<double>(ws, l.o_pmax), at<double>(ws, l.o_pss), s);
-  else
-    launch_row_stats(B, l.NF, l.K, l.bits, at<int16_t>(ws, l.o_sftB), at<float>(ws, l.o_lgB), s);
-  launch_maxlg(at<float>(ws, l.o_lgA), l.MF, at<float>(ws, l.o_lgB), l.NF, head->maxlg, s);
+  if (l.nt) {
+    launch_row_stats(A, l.MF, l.K, l.bits, at<int16_t>(ws, l.o_sftA), at<float>(ws, l.o_lgA), s);
+    launch_col_stats_maxlg(B, l.batch, l.K, l.N, l.kslab, l.nslab, l.bits, at<int16_t>(ws, l.o_sftB),
+                           at<float>(ws, l.o_lgB), at<double>(ws, l.o_pmax), at<double>(ws, l.o_pss),
+                           at<float>(ws, l.o_lgA), l.MF, head->maxlg, &head->counter, s);
+  } else {
+    launch_rows_stats_both(A, l.MF, B, l.NF, l.K, l.bits, at<int16_t>(ws, l.o_sftA), at<float>(ws, l.o_lgA),
+                           at<int16_t>(ws, l.o_sftB), at<float>(ws, l.o_lgB), head->maxlg, &head->counter, s);
+  }
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "sizing launch");
   return F64E_OK;
@@ -402,7 +405,7 @@ ExtractArgs extract_args(const Plan& l, void* ws, int64_t k0, int64_t kw) {
 }
 
 // Extraction of one K window [k0, k0 + kw) of A (planes [residues, hi, q]).
-void extract_A(const Plan& l, const ModTables& T, const View& v, void* ws, int64_t k0, int64_t kw, cudaStream_t s) {
+ExtractArgs extract_A_args(const Plan& l, const View& v, void* ws, int64_t k0, int64_t kw) {
   ExtractArgs ea = extract_args(l, ws, k0, kw);
   ea.X = v.A;
   ea.rows = v.batch * v.M;
@@ -413,11 +416,15 @@ void extract_A(const Plan& l, const ModTables& T, const View& v, void* ws, int64
   ea.q_plane = l.P + 1;
   ea.planes = v.pA;
   ea.pstride = ea.rows * l.Kp;
-  launch_extract_rows(ea, T, s);
+  return ea;
+}
+
+void extract_A(const Plan& l, const ModTables& T, const View& v, void* ws, int64_t k0, int64_t kw, cudaStream_t s) {
+  launch_extract_rows(extract_A_args(l, v, ws, k0, kw), T, s);
 }
 
 // Extraction of one K window of B (planes [residues, q, hi]).
-void extract_B(const Plan& l, const ModTables& T, const View& v, void* ws, int64_t k0, int64_t kw, cudaStream_t s) {
+ExtractArgs extract_B_args(const Plan& l, const View& v, void* ws, int64_t k0, int64_t kw) {
   ExtractArgs eb = extract_args(l, ws, k0, kw);
   eb.X = v.B;
   eb.rows = v.batch * v.N;
@@ -429,8 +436,25 @@ void extract_B(const Plan& l, const ModTables& T, const View& v, void* ws, int64
   eb.hi_plane = l.P + 1;
   eb.planes = v.pB;
   eb.pstride = v.batch * v.b_zrows * l.Kp;
+  return eb;
+}
+
+void extract_B(const Plan& l, const ModTables& T, const View& v, void* ws, int64_t k0, int64_t kw, cudaStream_t s) {
+  const ExtractArgs eb = extract_B_args(l, v, ws, k0, kw);
   if (l.nt) launch_extract_cols(eb, T, s);
   else launch_extract_rows(eb, T, s);
+}
+
+// Both operands of a view; one launch for two [rows, K] operands of a small
+// product (where launch latency, not the extraction, dominates).
+void extract_AB(const Plan& l, const ModTables& T, const View& v, void* ws, int64_t k0, int64_t kw, cudaStream_t s) {
+  constexpr int64_t kPairMaxElems = int64_t(1) << 22;
+  if (!l.nt && (v.batch * v.M + v.batch * v.N) * kw <= kPairMaxElems) {
+    launch_extract_rows_pair(extract_A_args(l, v, ws, k0, kw), extract_B_args(l, v, ws, k0, kw), T, s);
+    return;
+  }
+  extract_A(l, T, v, ws, k0, kw, s);
+  extract_B(l, T, v, ws, k0, kw, s);
 }
 
 GemmArgs gemm_args(const Plan& l, const View& v, void* ws) {
@@ -750,10 +774,7 @@ int run(const f64e_problem* p, const double* A, const double* B, double* out, vo
     }
   }
   if (!l.deep) {
-    if (phases & F64E_PHASE_EXTRACT) {
-      extract_A(l, T, f, ws, 0, l.K, s);
-      extract_B(l, T, f, ws, 0, l.K, s);
-    }
+    if (phases & F64E_PHASE_EXTRACT) extract_AB(l, T, f, ws, 0, l.K, s);
     if (ev) cudaEventRecord(ev[1], s);
     if (phases & F64E_PHASE_GEMM) {
       if (ngev >= 2) cudaEventRecord(static_cast<cudaEvent_t>(gev[0]), s);

@@ -175,8 +175,11 @@ __device__ __noinline__ uint32_t residue_word_ref(uint64_t u0, uint64_t u1, uint
 // [rows, K] operand: thread (x, y) of a (32, 8) block handles 8 consecutive
 // columns of one row; a warp covers 256 columns (2 KB read, 256 B written per
 // plane, both contiguous).
-template <bool VEC>
-__global__ void __launch_bounds__(256) extract_rows_kernel(const ExtractArgs a, const ModTables T) {
+// PAIR: two operands in one launch, blockIdx.z selecting the arguments
+// (small products, where launches dominate).
+template <bool VEC, bool PAIR>
+__global__ void __launch_bounds__(256) extract_rows_kernel(const ExtractPair ap, const ModTables T) {
+  const ExtractArgs& a = ap.a[PAIR ? blockIdx.z : 0];
   const Gain gn = pick_gain(a.maxlg[0], a.maxlg[1], T.log2M, a.bits);
   const int be = gn.bits_eff;
   const bool corr = a.use_corr != 0;
@@ -346,14 +349,38 @@ __global__ void __launch_bounds__(256, 4) extract_cols_kernel(const ExtractArgs 
   }
 }
 
+namespace {
+bool rows_vec(const ExtractArgs& a) {
+  return (a.ld % 2 == 0) && (a.koff % 2 == 0) && ((reinterpret_cast<uintptr_t>(a.X) & 15) == 0);
+}
+}  // namespace
+
 void launch_extract_rows(const ExtractArgs& a, const ModTables& T, cudaStream_t s) {
   if (a.rows <= 0 || a.Kp <= 0) return;
   const int64_t nch = a.Kp >> 3;
   const unsigned gx = (unsigned)std::min<int64_t>((nch + 31) / 32, 1 << 20);
   const unsigned gy = (unsigned)std::min<int64_t>((a.rows + 7) / 8, 65535);
-  const bool vec = (a.ld % 2 == 0) && (a.koff % 2 == 0) && ((reinterpret_cast<uintptr_t>(a.X) & 15) == 0);
-  if (vec) extract_rows_kernel<true><<<dim3(gx, gy), dim3(32, 8), 0, s>>>(a, T);
-  else extract_rows_kernel<false><<<dim3(gx, gy), dim3(32, 8), 0, s>>>(a, T);
+  ExtractPair ap;
+  ap.a[0] = a;
+  ap.a[1] = a;
+  if (rows_vec(a)) extract_rows_kernel<true, false><<<dim3(gx, gy), dim3(32, 8), 0, s>>>(ap, T);
+  else extract_rows_kernel<false, false><<<dim3(gx, gy), dim3(32, 8), 0, s>>>(ap, T);
+}
+
+void launch_extract_rows_pair(const ExtractArgs& a0, const ExtractArgs& a1, const ModTables& T, cudaStream_t s) {
+  if (a0.rows <= 0 || a1.rows <= 0 || a0.Kp <= 0) {
+    launch_extract_rows(a0, T, s);
+    launch_extract_rows(a1, T, s);
+    return;
+  }
+  const int64_t nch = a0.Kp >> 3;
+  const unsigned gx = (unsigned)std::min<int64_t>((nch + 31) / 32, 1 << 20);
+  const unsigned gy = (unsigned)std::min<int64_t>((std::max(a0.rows, a1.rows) + 7) / 8, 65535);
+  ExtractPair ap;
+  ap.a[0] = a0;
+  ap.a[1] = a1;
+  if (rows_vec(a0) && rows_vec(a1)) extract_rows_kernel<true, true><<<dim3(gx, gy, 2), dim3(32, 8), 0, s>>>(ap, T);
+  else extract_rows_kernel<false, true><<<dim3(gx, gy, 2), dim3(32, 8), 0, s>>>(ap, T);
 }
 
 void launch_extract_cols(const ExtractArgs& a, const ModTables& T, cudaStream_t s) {

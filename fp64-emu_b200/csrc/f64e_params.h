@@ -1,6 +1,6 @@
 // Parameter blocks shared by the host orchestration and the fp64-emu kernels.
 // Everything a kernel needs about the modulus set travels by value in
-// ModTables (under 2 KB of kernel-parameter space), so no call ever uploads
+// ModTables (under 3 KB of kernel-parameter space), so no call ever uploads
 // tables or keeps per-device caches: every launch is capture-safe.
 #pragma once
 
@@ -53,8 +53,8 @@ struct ModTables {
 // phases, so every rank derives the same operand width.
 struct WsHead {
   float maxlg[2];
-  int32_t status;  // first bounded wait that timed out (0 = none)
-  int32_t pad;
+  int32_t status;    // first bounded wait that timed out (0 = none)
+  uint32_t counter;  // CTAs done in the current sizing launch (zeroed with status)
 };
 
 }  // namespace f64e

@@ -21,57 +21,122 @@ __device__ __forceinline__ void finish_stats(double m, double s2, int bits, int1
   *sft = (int16_t)sh;
 }
 
-// One CTA of 256 threads per row.  Loads are issued four ahead; the
-// accumulation order per thread is the plain strided order.
-__global__ void __launch_bounds__(256) row_stats_kernel(const double* __restrict__ X, int64_t rows,
-                                                        int64_t cols, int bits, int16_t* __restrict__ sft,
-                                                        float* __restrict__ lg) {
-  for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
-    const double* __restrict__ x = X + r * cols;
-    double mx = 0.0, ss = 0.0;
-    int64_t c = threadIdx.x;
-    for (; c + 768 < cols; c += 1024) {
-      const double v0 = __ldg(x + c), v1 = __ldg(x + c + 256), v2 = __ldg(x + c + 512), v3 = __ldg(x + c + 768);
-      mx = fmax(mx, fabs(v0));
-      ss = fma(v0, v0, ss);
-      mx = fmax(mx, fabs(v1));
-      ss = fma(v1, v1, ss);
-      mx = fmax(mx, fabs(v2));
-      ss = fma(v2, v2, ss);
-      mx = fmax(mx, fabs(v3));
-      ss = fma(v3, v3, ss);
-    }
-    for (; c < cols; c += 256) {
-      const double v = __ldg(x + c);
-      mx = fmax(mx, fabs(v));
-      ss = fma(v, v, ss);
-    }
-    __shared__ double sm[256], sq[256];
-    const int t = threadIdx.x;
-    sm[t] = mx;
-    sq[t] = ss;
-    __syncthreads();
+// Statistics of one row by one CTA of 256 threads.  Loads are issued four
+// ahead; the accumulation order per thread is the plain strided order.
+__device__ __forceinline__ void row_stats_one(const double* __restrict__ x, int64_t cols, int bits,
+                                              int16_t* __restrict__ sft, float* __restrict__ lg) {
+  double mx = 0.0, ss = 0.0;
+  int64_t c = threadIdx.x;
+  for (; c + 768 < cols; c += 1024) {
+    const double v0 = __ldg(x + c), v1 = __ldg(x + c + 256), v2 = __ldg(x + c + 512), v3 = __ldg(x + c + 768);
+    mx = fmax(mx, fabs(v0));
+    ss = fma(v0, v0, ss);
+    mx = fmax(mx, fabs(v1));
+    ss = fma(v1, v1, ss);
+    mx = fmax(mx, fabs(v2));
+    ss = fma(v2, v2, ss);
+    mx = fmax(mx, fabs(v3));
+    ss = fma(v3, v3, ss);
+  }
+  for (; c < cols; c += 256) {
+    const double v = __ldg(x + c);
+    mx = fmax(mx, fabs(v));
+    ss = fma(v, v, ss);
+  }
+  __shared__ double sm[256], sq[256];
+  const int t = threadIdx.x;
+  sm[t] = mx;
+  sq[t] = ss;
+  __syncthreads();
 #pragma unroll
-    for (int s = 128; s >= 32; s >>= 1) {
-      if (t < s) {
-        sm[t] = fmax(sm[t], sm[t + s]);
-        sq[t] += sq[t + s];
-      }
-      __syncthreads();
-    }
-    if (t < 32) {
-      double m = sm[t], q = sq[t];
-#pragma unroll
-      for (int s = 16; s > 0; s >>= 1) {
-        const double mo = __shfl_down_sync(0xFFFFFFFFu, m, s);
-        const double qo = __shfl_down_sync(0xFFFFFFFFu, q, s);
-        m = fmax(m, mo);
-        q += qo;
-      }
-      if (t == 0) finish_stats(m, q, bits, &sft[r], &lg[r]);
+  for (int s = 128; s >= 32; s >>= 1) {
+    if (t < s) {
+      sm[t] = fmax(sm[t], sm[t + s]);
+      sq[t] += sq[t + s];
     }
     __syncthreads();
   }
+  if (t < 32) {
+    double m = sm[t], q = sq[t];
+#pragma unroll
+    for (int s = 16; s > 0; s >>= 1) {
+      const double mo = __shfl_down_sync(0xFFFFFFFFu, m, s);
+      const double qo = __shfl_down_sync(0xFFFFFFFFu, q, s);
+      m = fmax(m, mo);
+      q += qo;
+    }
+    if (t == 0) finish_stats(m, q, bits, sft, lg);
+  }
+  __syncthreads();
+}
+
+__global__ void __launch_bounds__(256) row_stats_kernel(const double* __restrict__ X, int64_t rows,
+                                                        int64_t cols, int bits, int16_t* __restrict__ sft,
+                                                        float* __restrict__ lg) {
+  for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) row_stats_one(X + r * cols, cols, bits, &sft[r], &lg[r]);
+}
+
+// Operand maxima of lg over both operands by one CTA of 256 threads (max is
+// order independent), written to out[0..1].
+__device__ __forceinline__ void maxlg_block(const float* lgA, int64_t m, const float* lgB, int64_t n, float* out) {
+  float a = -INFINITY, b = -INFINITY;
+  for (int64_t i = threadIdx.x; i < m; i += blockDim.x) a = fmaxf(a, __ldcg(lgA + i));
+  for (int64_t j = threadIdx.x; j < n; j += blockDim.x) b = fmaxf(b, __ldcg(lgB + j));
+#pragma unroll
+  for (int s = 16; s > 0; s >>= 1) {
+    a = fmaxf(a, __shfl_xor_sync(0xFFFFFFFFu, a, s));
+    b = fmaxf(b, __shfl_xor_sync(0xFFFFFFFFu, b, s));
+  }
+  __shared__ float sa[32], sb[32];
+  if ((threadIdx.x & 31) == 0) {
+    sa[threadIdx.x >> 5] = a;
+    sb[threadIdx.x >> 5] = b;
+  }
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    const int nw = blockDim.x >> 5;
+    a = threadIdx.x < nw ? sa[threadIdx.x] : -INFINITY;
+    b = threadIdx.x < nw ? sb[threadIdx.x] : -INFINITY;
+#pragma unroll
+    for (int s = 16; s > 0; s >>= 1) {
+      a = fmaxf(a, __shfl_xor_sync(0xFFFFFFFFu, a, s));
+      b = fmaxf(b, __shfl_xor_sync(0xFFFFFFFFu, b, s));
+    }
+    if (threadIdx.x == 0) {
+      out[0] = a;
+      out[1] = b;
+    }
+  }
+}
+
+// True in every thread of the CTA that finishes last among gridDim.x CTAs
+// (counter zeroed before the launch).  The caller's results are published by
+// the fence before the count, so the last CTA sees every CTA's writes.
+__device__ __forceinline__ bool last_block_done(unsigned* counter) {
+  __shared__ bool last;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    last = atomicAdd(counter, 1u) == gridDim.x - 1;
+  }
+  __syncthreads();
+  if (last) __threadfence();
+  return last;
+}
+
+// Both operands in the [rows, K] layout in one launch: CTAs take A's rows,
+// then B's; the last CTA to finish takes the operand maxima.
+__global__ void __launch_bounds__(256) rows_stats_both_kernel(const double* __restrict__ A, int64_t ra,
+                                                              const double* __restrict__ B, int64_t rb,
+                                                              int64_t cols, int bits, int16_t* __restrict__ sftA,
+                                                              float* __restrict__ lgA, int16_t* __restrict__ sftB,
+                                                              float* __restrict__ lgB, float* __restrict__ maxlg,
+                                                              unsigned* __restrict__ counter) {
+  for (int64_t r = blockIdx.x; r < ra + rb; r += gridDim.x) {
+    if (r < ra) row_stats_one(A + r * cols, cols, bits, &sftA[r], &lgA[r]);
+    else row_stats_one(B + (r - ra) * cols, cols, bits, &sftB[r - ra], &lgB[r - ra]);
+  }
+  if (last_block_done(counter)) maxlg_block(lgA, ra, lgB, rb, maxlg);
 }
 
 // Column partials over one K slab per blockIdx.y: thread j owns global column
@@ -108,52 +173,23 @@ __global__ void __launch_bounds__(256) col_partial_kernel(const double* __restri
   pss[(int64_t)blockIdx.y * totalcols + j] = ss;
 }
 
-__global__ void __launch_bounds__(256) col_finalize_kernel(const double* __restrict__ pmax,
-                                                           const double* __restrict__ pss, int64_t totalcols,
-                                                           int nslab, int bits, int16_t* __restrict__ sft,
-                                                           float* __restrict__ lg) {
+// Column finalize of B plus the operand maxima by the last CTA to finish.
+__global__ void __launch_bounds__(256) col_finalize_maxlg_kernel(const double* __restrict__ pmax,
+                                                                 const double* __restrict__ pss, int64_t totalcols,
+                                                                 int nslab, int bits, int16_t* __restrict__ sft,
+                                                                 float* __restrict__ lg, const float* lgA,
+                                                                 int64_t ra, float* __restrict__ maxlg,
+                                                                 unsigned* __restrict__ counter) {
   const int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (j >= totalcols) return;
-  double mx = 0.0, ss = 0.0;
-  for (int s = 0; s < nslab; s++) {
-    mx = fmax(mx, pmax[(int64_t)s * totalcols + j]);
-    ss += pss[(int64_t)s * totalcols + j];
-  }
-  finish_stats(mx, ss, bits, &sft[j], &lg[j]);
-}
-
-// Operand maxima of lg (max is order independent).  One CTA.
-__global__ void __launch_bounds__(1024) maxlg_kernel(const float* __restrict__ lgA, int64_t m,
-                                                     const float* __restrict__ lgB, int64_t n,
-                                                     float* __restrict__ out) {
-  float a = -INFINITY, b = -INFINITY;
-  for (int64_t i = threadIdx.x; i < m; i += blockDim.x) a = fmaxf(a, lgA[i]);
-  for (int64_t j = threadIdx.x; j < n; j += blockDim.x) b = fmaxf(b, lgB[j]);
-#pragma unroll
-  for (int s = 16; s > 0; s >>= 1) {
-    a = fmaxf(a, __shfl_xor_sync(0xFFFFFFFFu, a, s));
-    b = fmaxf(b, __shfl_xor_sync(0xFFFFFFFFu, b, s));
-  }
-  __shared__ float sa[32], sb[32];
-  if ((threadIdx.x & 31) == 0) {
-    sa[threadIdx.x >> 5] = a;
-    sb[threadIdx.x >> 5] = b;
-  }
-  __syncthreads();
-  if (threadIdx.x < 32) {
-    const int nw = blockDim.x >> 5;
-    a = threadIdx.x < nw ? sa[threadIdx.x] : -INFINITY;
-    b = threadIdx.x < nw ? sb[threadIdx.x] : -INFINITY;
-#pragma unroll
-    for (int s = 16; s > 0; s >>= 1) {
-      a = fmaxf(a, __shfl_xor_sync(0xFFFFFFFFu, a, s));
-      b = fmaxf(b, __shfl_xor_sync(0xFFFFFFFFu, b, s));
+  if (j < totalcols) {
+    double mx = 0.0, ss = 0.0;
+    for (int s = 0; s < nslab; s++) {
+      mx = fmax(mx, pmax[(int64_t)s * totalcols + j]);
+      ss += pss[(int64_t)s * totalcols + j];
     }
-    if (threadIdx.x == 0) {
-      out[0] = a;
-      out[1] = b;
-    }
+    finish_stats(mx, ss, bits, &sft[j], &lg[j]);
   }
+  if (last_block_done(counter)) maxlg_block(lgA, ra, lg, totalcols, maxlg);
 }
 
 void launch_row_stats(const double* X, int64_t rows, int64_t cols, int bits, int16_t* sft, float* lg,
@@ -170,17 +206,20 @@ void col_slabs(int64_t NF, int64_t K, int64_t* kslab, int* nslab) {
   *nslab = *kslab > 0 ? (int)((K + *kslab - 1) / *kslab) : 0;
 }
 
-void launch_col_stats(const double* X, int64_t batch, int64_t K, int64_t N, int64_t kslab, int nslab, int bits,
-                      int16_t* sft, float* lg, double* pmax, double* pss, cudaStream_t s) {
-  const int64_t NF = batch * N;
-  if (NF <= 0) return;
-  const unsigned gx = (unsigned)((NF + 255) / 256);
-  if (nslab > 0) col_partial_kernel<<<dim3(gx, nslab), 256, 0, s>>>(X, NF, K, N, kslab, pmax, pss);
-  col_finalize_kernel<<<gx, 256, 0, s>>>(pmax, pss, NF, nslab, bits, sft, lg);
+void launch_rows_stats_both(const double* A, int64_t ra, const double* B, int64_t rb, int64_t cols, int bits,
+                            int16_t* sftA, float* lgA, int16_t* sftB, float* lgB, float* maxlg, unsigned* counter,
+                            cudaStream_t s) {
+  const unsigned grid = (unsigned)std::max<int64_t>(1, std::min<int64_t>(ra + rb, 1 << 30));
+  rows_stats_both_kernel<<<grid, 256, 0, s>>>(A, ra, B, rb, cols, bits, sftA, lgA, sftB, lgB, maxlg, counter);
 }
 
-void launch_maxlg(const float* lgA, int64_t m, const float* lgB, int64_t n, float* out, cudaStream_t s) {
-  maxlg_kernel<<<1, 1024, 0, s>>>(lgA, m, lgB, n, out);
+void launch_col_stats_maxlg(const double* X, int64_t batch, int64_t K, int64_t N, int64_t kslab, int nslab,
+                            int bits, int16_t* sft, float* lg, double* pmax, double* pss, const float* lgA,
+                            int64_t ra, float* maxlg, unsigned* counter, cudaStream_t s) {
+  const int64_t NF = batch * N;
+  const unsigned gx = (unsigned)std::max<int64_t>(1, (NF + 255) / 256);
+  if (nslab > 0 && NF > 0) col_partial_kernel<<<dim3(gx, nslab), 256, 0, s>>>(X, NF, K, N, kslab, pmax, pss);
+  col_finalize_maxlg_kernel<<<gx, 256, 0, s>>>(pmax, pss, NF, nslab, bits, sft, lg, lgA, ra, maxlg, counter);
 }
 
 }  // namespace f64e

@@ -2,7 +2,10 @@
 call and native cuBLAS DGEMM, for n where launch overhead dominates (the
 reference measures the same in bench/smalln.py of fp64-emu).
 
-    python fp64-emu_b200/smalln.py [n ...]
+    python fp64-emu_b200/smalln.py [--reference] [n ...]
+
+--reference times the reference's own build (oracle/_ref, compiled from its
+sources) through its own Python API instead, for comparison.
 
 Prints one JSON line: per n the median wall time (µs) of each, and whether the
 graph replay's result equals the eager one bit for bit.
@@ -33,8 +36,18 @@ def median_us(fn, iters=200, warm=20):
     return statistics.median(ts) * 1e6
 
 
-def measure(n):
-    import fp64_emu
+def load(reference):
+    if not reference:
+        import fp64_emu
+        return fp64_emu
+    ref = os.path.join(os.path.dirname(HERE), "oracle", "_ref")
+    if ref not in sys.path:
+        sys.path.insert(0, ref)
+    import fp64_emu_ref
+    return fp64_emu_ref
+
+
+def measure(n, fp64_emu):
     gen = torch.Generator(device="cuda").manual_seed(n)
     A = torch.randn(n, n, dtype=torch.float64, device="cuda", generator=gen)
     B = torch.randn(n, n, dtype=torch.float64, device="cuda", generator=gen)
@@ -43,21 +56,28 @@ def measure(n):
     for _ in range(3):
         fp64_emu.mm(A, B)
     torch.cuda.synchronize()
-    g = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(g):
-        C = fp64_emu.mm(A, B)
-    g.replay()
-    torch.cuda.synchronize()
-    same = bool(torch.equal(C, fp64_emu.mm(A, B)))
-    graph = median_us(g.replay)
-    return {"n": n, "eager_us": round(eager, 1), "graph_us": round(graph, 1), "native_us": round(native, 1),
+    try:
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            C = fp64_emu.mm(A, B)
+        g.replay()
+        torch.cuda.synchronize()
+        same = bool(torch.equal(C, fp64_emu.mm(A, B)))
+        graph = round(median_us(g.replay), 1)
+    except Exception as e:  # noqa: BLE001  (a build whose call cannot be captured)
+        same, graph = None, f"capture failed: {type(e).__name__}"
+    return {"n": n, "eager_us": round(eager, 1), "graph_us": graph, "native_us": round(native, 1),
             "graph_equal": same}
 
 
 def main():
-    ns = [int(x) for x in sys.argv[1:]] or [64, 128, 256, 512]
-    rows = [measure(n) for n in ns]
-    print(json.dumps({"device": torch.cuda.get_device_name(0), "smalln": rows}), flush=True)
+    args = sys.argv[1:]
+    reference = "--reference" in args
+    ns = [int(x) for x in args if x != "--reference"] or [64, 128, 256, 512]
+    emu = load(reference)
+    rows = [measure(n, emu) for n in ns]
+    print(json.dumps({"device": torch.cuda.get_device_name(0), "impl": "reference" if reference else "ours",
+                      "smalln": rows}), flush=True)
 
 
 if __name__ == "__main__":

@@ -165,6 +165,41 @@ int get_tables(const int32_t* primes, int P, ModTables* out) {
     for (int t = std::min(g * 7 + 6, P - 1); t >= g * 7; t--) hv = hv * primes[t] + primes[t] / 2;
     T.hoff[g] = hv;
   }
+  // Direct CRT constants (see ModTables), for products of the moduli below 2^121.
+  {
+    using u128 = unsigned __int128;
+    u128 M = 1;
+    bool ok = true;
+    for (int t = 0; t < P && ok; t++) {
+      if (M > ((u128)1 << 121) / (u128)primes[t]) ok = false;
+      else M *= (u128)primes[t];
+    }
+    T.crt_ok = ok ? 1 : 0;
+    if (ok) {
+      for (int t = 0; t < P; t++) {
+        const u128 Mt = M / (u128)primes[t];
+        const int y = modinv_small((int)(Mt % (u128)primes[t]), primes[t]);
+        const u128 E = Mt * (u128)y;   // < M
+        for (int i = 0; i < 4; i++) T.crtE[t][i] = (uint32_t)(E >> (32 * i));
+      }
+      for (int i = 0; i < 4; i++) T.crtM[i] = (uint32_t)(M >> (32 * i));
+      const long double Md = (long double)M;
+      T.crtK96 = (double)(std::ldexp(1.0L, 96) / Md);
+      T.crtK32 = (double)(std::ldexp(1.0L, 32) / Md);
+      T.crtK0 = (double)(1.0L / Md);
+      // low end of the balanced mixed-radix range: sum_t dmin_t * (p_0 ... p_{t-1}),
+      // dmin_t = -floor(p_t / 2) (the digit range of a balanced residue)
+      u128 run = 1, negL = 0;
+      for (int t = 0; t < P; t++) {
+        negL += (u128)(primes[t] / 2) * run;
+        run *= (u128)primes[t];
+      }
+      T.crt_c = (double)((long double)negL / Md);
+      const u128 L = (u128)0 - negL;
+      T.crtL[0] = (uint64_t)L;
+      T.crtL[1] = (uint64_t)(L >> 64);
+    }
+  }
   cache.emplace(key, T);
   *out = T;
   return F64E_OK;

@@ -45,6 +45,18 @@ struct ModTables {
   int64_t hoff[3];             // Horner value of the offsets h per 7-modulus group
   uint64_t wgrp[kMaxP];        // radix weight of digit t inside its 7-modulus group
   int fast_recon;              // every modulus > 128
+
+  // Direct CRT form (M = prod p_t < 2^121): V = S - q M with S = sum u_t E_t,
+  // u_t the canonical residue, E_t = (M / p_t) * ((M / p_t)^-1 mod p_t) in
+  // four 32-bit limbs, q = floor(S / M + crt_c) from a double estimate (exact
+  // away from ties; ties take the digit-by-digit path).  crt_c = -L / M for
+  // L, the low end of the balanced mixed-radix range of this modulus order.
+  int crt_ok;
+  uint32_t crtE[kMaxP][4];
+  uint32_t crtM[4];
+  double crtK96, crtK32, crtK0;  // 2^96 / M, 2^32 / M, 1 / M
+  double crt_c;
+  uint64_t crtL[2];            // L as a 128-bit two's complement (lo, hi)
 };
 
 // Device-resident scalars at the head of every workspace.  maxlg holds the

@@ -11,6 +11,8 @@
 // rounds the 128-bit value once to double, the fast mode combines in fp64 with
 // the reference's fused multiply-adds.  The result is scaled by
 // 2^-(sA_i + sB_j).
+#include <cstdlib>
+
 #include "f64e_device.cuh"
 #include "f64e_kernels.h"
 
@@ -332,12 +334,124 @@ __global__ void __launch_bounds__(256, 2) reconstruct_fast_kernel(const ReconArg
   }
 }
 
+
+// Direct CRT form (exact mode, every modulus set with M < 2^121).  With u_t
+// the canonical residue (the stored balanced residue plus p_t when negative),
+// S = sum_t u_t E_t is the sum of four 32-bit limb products per modulus, and
+// the balanced Garner value is the representative V = S - q M in [L, L + M)
+// (L the low end of the balanced mixed-radix range, for every modulus
+// order).  q = floor(S / M - L / M) comes from a double estimate whose error
+// is below 2^-40; when the estimate lies within 2^-20 of an integer, V is
+// moved into [L, L + M) by exact 128-bit comparisons.  The value is the
+// Garner value bit for bit, so the rounding that follows is unchanged.
+__device__ __noinline__ I128 crt_fix(I128 v, uint64_t Llo, uint64_t Lhi, uint64_t Mlo, uint64_t Mhi) {
+  // w = v - L
+  const uint64_t wlo = v.lo - Llo;
+  const int64_t whi = (int64_t)((uint64_t)v.hi - Lhi - (v.lo < Llo ? 1ULL : 0ULL));
+  if (whi < 0) {   // v < L: one M up
+    const uint64_t lo = v.lo + Mlo;
+    v.hi = (int64_t)((uint64_t)v.hi + Mhi + (lo < Mlo ? 1ULL : 0ULL));
+    v.lo = lo;
+  } else if ((uint64_t)whi > Mhi || ((uint64_t)whi == Mhi && wlo >= Mlo)) {   // v >= L + M: one M down
+    const uint64_t lo = v.lo - Mlo;
+    v.hi = (int64_t)((uint64_t)v.hi - Mhi - (v.lo < Mlo ? 1ULL : 0ULL));
+    v.lo = lo;
+  }
+  return v;
+}
+
+template <int CM>
+__global__ void __launch_bounds__(256, 4) reconstruct_crt_kernel(const ReconArgs a, const ModTables T) {
+  const Gain gn = pick_gain(a.maxlg[0], a.maxlg[1], T.log2M, a.bits);
+  const int cshift = gn.bits_eff - 15;
+  const int P = T.P;
+  const int64_t nq = (a.N + 3) >> 2;
+  const int64_t plane = a.MF * a.ldn;
+  const bool vec_out = ((a.ldc & 3) == 0) && ((reinterpret_cast<uintptr_t>(a.C) & 15) == 0);
+  const uint64_t Mlo = ((uint64_t)T.crtM[1] << 32) | T.crtM[0], Mhi = ((uint64_t)T.crtM[3] << 32) | T.crtM[2];
+  for (int64_t i = (int64_t)blockIdx.y * 4 + threadIdx.y; i < a.MF; i += (int64_t)gridDim.y * 4) {
+    const int sa = (int)a.sftA[i] + gn.g;
+    const int16_t* __restrict__ sB = a.sftB + (a.M == a.MF ? 0 : (i / a.M) * a.N);
+    for (int64_t jq = (int64_t)blockIdx.x * 64 + threadIdx.x; jq < nq; jq += (int64_t)gridDim.x * 64) {
+      const int64_t j0 = jq << 2;
+      const int64_t off = i * a.ldn + j0;
+      uint32_t rw[kMaxP];
+#pragma unroll
+      for (int t = 0; t < kMaxP; t++)
+        rw[t] = (t < P) ? __ldg(reinterpret_cast<const unsigned int*>(a.res + t * plane + off)) : 0u;
+      int64_t cr[4];
+      load_corr<CM>(a, off, plane, cr);
+      double outv[4];
+#pragma unroll
+      for (int e = 0; e < 4; e++) {
+        uint64_t acc[4] = {0, 0, 0, 0};
+#pragma unroll
+        for (int t = 0; t < kMaxP; t++) {
+          if (t >= P) break;
+          const uint32_t p = T.p[t];
+          const int r = (int)(int8_t)(uint8_t)(rw[t] >> (8 * e));
+          const uint32_t u = (uint32_t)r + ((uint32_t)(r >> 31) & p);
+#pragma unroll
+          for (int l = 0; l < 4; l++) acc[l] += (uint64_t)u * T.crtE[t][l];
+        }
+        // S in five 32-bit limbs
+        const uint32_t s0 = (uint32_t)acc[0];
+        const uint64_t t1 = acc[1] + (acc[0] >> 32);
+        const uint64_t t2 = acc[2] + (t1 >> 32);
+        const uint64_t t3 = acc[3] + (t2 >> 32);
+        const uint32_t s1 = (uint32_t)t1, s2 = (uint32_t)t2, s3 = (uint32_t)t3, s4 = (uint32_t)(t3 >> 32);
+        const double x = __ull2double_rn(((uint64_t)s4 << 32) | s3) * T.crtK96 +
+                         __ull2double_rn(((uint64_t)s2 << 32) | s1) * T.crtK32 + (double)s0 * T.crtK0 + T.crt_c;
+        const double fq = floor(x);
+        const uint32_t q = (uint32_t)fq;
+        const double fr = x - fq;
+        // V = S - q M modulo 2^128 (the true V lies in [L, L + M), |V| < 2^121)
+        const uint64_t qm0 = (uint64_t)q * T.crtM[0];
+        const uint64_t qm1 = (uint64_t)q * T.crtM[1] + (qm0 >> 32);
+        const uint64_t qm2 = (uint64_t)q * T.crtM[2] + (qm1 >> 32);
+        const uint64_t qm3 = (uint64_t)q * T.crtM[3] + (qm2 >> 32);
+        const uint64_t Slo = ((uint64_t)s1 << 32) | s0, Shi = ((uint64_t)s3 << 32) | s2;
+        const uint64_t QMlo = (qm1 << 32) | (uint32_t)qm0, QMhi = (qm3 << 32) | (uint32_t)qm2;
+        I128 v;
+        v.lo = Slo - QMlo;
+        v.hi = (int64_t)(Shi - QMhi - (Slo < QMlo ? 1ULL : 0ULL));
+        if (fr < 0x1p-20 || fr > 1.0 - 0x1p-20) v = crt_fix(v, T.crtL[0], T.crtL[1], Mlo, Mhi);
+        const int64_t j = j0 + e;
+        const int sh = -sa - (j < a.N ? (int)sB[j] + gn.g : 0);
+        if (CM != 0) v = i128_add_shl(v, cr[e], cshift);
+        outv[e] = i128_to_double_scaled(v, sh);
+      }
+      double* crow = a.C + i * a.ldc;
+      if (vec_out && j0 + 4 <= a.N) {
+        *reinterpret_cast<double2*>(crow + j0) = make_double2(outv[0], outv[1]);
+        *reinterpret_cast<double2*>(crow + j0 + 2) = make_double2(outv[2], outv[3]);
+      } else {
+#pragma unroll
+        for (int e = 0; e < 4; e++)
+          if (j0 + e < a.N) crow[j0 + e] = outv[e];
+      }
+    }
+  }
+}
+
 void launch_reconstruct(const ReconArgs& a, const ModTables& T, cudaStream_t s) {
   if (a.MF <= 0 || a.N <= 0) return;
   const int64_t nq = (a.N + 3) >> 2;
   const dim3 grid((unsigned)std::min<int64_t>((nq + 63) / 64, 1 << 20),
                   (unsigned)std::min<int64_t>((a.MF + 3) / 4, 65535));
   const dim3 block(64, 4);
+  // F64E_RECON_GARNER=1 keeps exact products on the digit-by-digit kernels
+  // (A/B checks of the direct CRT form); read per call.
+  const char* gv = std::getenv("F64E_RECON_GARNER");
+  if (a.exact && T.crt_ok && !(gv && gv[0] == '1')) {
+    switch (a.corr_mode) {
+      case 0: reconstruct_crt_kernel<0><<<grid, block, 0, s>>>(a, T); break;
+      case 1: reconstruct_crt_kernel<1><<<grid, block, 0, s>>>(a, T); break;
+      case 2: reconstruct_crt_kernel<2><<<grid, block, 0, s>>>(a, T); break;
+      default: reconstruct_crt_kernel<3><<<grid, block, 0, s>>>(a, T); break;
+    }
+    return;
+  }
   if (T.fast_recon) {
     if (a.exact) {
       switch (a.corr_mode) {

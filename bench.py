@@ -596,7 +596,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="C2", choices=sorted(WORKLOADS))
     ap.add_argument("--seed", type=int, default=0)
-    ap.add_argument("--cpu-rows", type=int, default=512)
+    ap.add_argument("--cpu-rows", type=int, default=1024)
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baselines")
     ap.add_argument("--no-native", action="store_true", help="skip the cuBLAS DGEMM context number")
     args = ap.parse_args()

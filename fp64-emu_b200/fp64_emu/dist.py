@@ -116,6 +116,24 @@ def bmm_nt_sharded(A_b, Bt_b, batch_total, group=None, **kw):
     return ShardedProduct(A_b, Bt_b, True, batch_total * Bt_b.size(2), A_b.size(2), group=group, **kw).run(out)
 
 
+def host_share_ranges(rank, world, M, N, K, b_kn):
+    """The host shares rank copies in for a ShardedHostStream product: the
+    global rows [a0, a1) of A (a slice of its row block, split over the pc
+    ranks of its grid row, ceil-sized so only the last slices are short) and
+    the range [b0, b1) of the first dimension of B's column block ([K, nb]
+    when b_kn, else [nb, K]), split over the pr ranks of its grid column."""
+    pr, pc = grid_shape(world)
+    gi, gj = divmod(rank, pc)
+    (r0, r1), (c0, c1) = rank_block(rank, world, M, N)
+    mb, nb = r1 - r0, c1 - c0
+    a_rows = -(-mb // pc)
+    a0 = min(mb, gj * a_rows)
+    ext = K if b_kn else nb
+    b_rows = -(-ext // pr)
+    b0 = min(ext, gi * b_rows)
+    return (r0 + a0, r0 + min(mb, a0 + a_rows)), (b0, min(ext, b0 + b_rows))
+
+
 class ShardedHostStream:
     """A stream of partitioned products whose operands and results live in host
     memory, one process per GPU.
@@ -166,14 +184,11 @@ class ShardedHostStream:
 
     def a_share_range(self):
         """Rows of A (global indices) this rank copies in."""
-        a0 = min(self.mb, self.gj * self.a_rows)
-        return self.r0 + a0, self.r0 + min(self.mb, a0 + self.a_rows)
+        return host_share_ranges(self.rank, self.world, self.M, self.N, self.K, self.b_kn)[0]
 
     def b_share_range(self):
         """First-dimension range of B's column block ([K, nb] or [nb, K]) this rank copies in."""
-        ext = self.K if self.b_kn else self.nb
-        b0 = min(ext, self.gi * self.b_rows)
-        return b0, min(ext, b0 + self.b_rows)
+        return host_share_ranges(self.rank, self.world, self.M, self.N, self.K, self.b_kn)[1]
 
     def host_shares(self, A, B):
         """This rank's page-locked shares of full host operands A [M, K] and

@@ -122,3 +122,27 @@ def test_grid_shapes():
     for (r0, r1), (c0, c1) in blocks:
         cover[r0 // 1024:r1 // 1024, c0 // 1024:c1 // 1024] += 1
     assert (cover == 1).all()
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+@pytest.mark.parametrize("shape", [(8192, 8192, 8192), (700, 900, 1500), (5, 3, 17), (1030, 520, 333)])
+@pytest.mark.parametrize("b_kn", [True, False])
+def test_host_share_ranges_partition_each_block(world, shape, b_kn):
+    # the host shares of the ranks of one grid row tile that row's block of A,
+    # and those of one grid column tile that column's block of B, exactly once
+    from fp64_emu.dist import grid_shape, host_share_ranges, rank_block
+    M, N, K = shape
+    pr, pc = grid_shape(world)
+    for i in range(pr):
+        ranks = [i * pc + j for j in range(pc)]
+        (r0, r1), _ = rank_block(ranks[0], world, M, N)
+        rows = sorted(host_share_ranges(r, world, M, N, K, b_kn)[0] for r in ranks)
+        covered = [x for a0, a1 in rows for x in range(a0, a1)]
+        assert covered == list(range(r0, r1))
+    for j in range(pc):
+        ranks = [i * pc + j for i in range(pr)]
+        _, (c0, c1) = rank_block(ranks[0], world, M, N)
+        ext = K if b_kn else c1 - c0
+        parts = sorted(host_share_ranges(r, world, M, N, K, b_kn)[1] for r in ranks)
+        covered = [x for b0, b1 in parts for x in range(b0, b1)]
+        assert covered == list(range(ext))

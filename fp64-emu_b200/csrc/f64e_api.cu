@@ -637,6 +637,7 @@ struct Chunking {
   bool by_batch = false;
   int64_t per = 0;    // rows (or members) per chunk; 0 = unchunked
   int64_t cols = 0;   // columns per block of the first row chunk; 0 = whole
+  std::vector<int64_t> bounds;   // chunk boundaries 0 = b_0 < b_1 < ... < b_C = extent
 };
 
 Chunking pipe_chunking(const Plan& l) {
@@ -670,17 +671,42 @@ Chunking pipe_chunking(const Plan& l) {
     if (c.cols > 0) c.cols = round_up(c.cols, 16);
     if (c.cols >= l.N) c.cols = 0;
   }
+  // Boundaries.  Single products of at least three chunks start and end with
+  // half-size chunks (the first one's extraction and the last one's
+  // reconstruction are the parts no GEMM runs beside); F64E_PIPE_ENDS=0 keeps
+  // every chunk the same size.
+  c.bounds.assign(1, 0);
+  const int64_t ends = env_int("F64E_PIPE_ENDS");
+  const int64_t half = round_up((c.per + 1) / 2, 256);
+  if (!c.by_batch && ends != 0 && c.per >= 1024 && extent >= 3 * c.per) {
+    int64_t at = half;
+    c.bounds.push_back(at);
+    while (extent - at > c.per + half) {
+      at += c.per;
+      c.bounds.push_back(at);
+    }
+    if (extent - at > half) c.bounds.push_back(extent - half);
+    c.bounds.push_back(extent);
+  } else {
+    for (int64_t at = c.per; at < extent; at += c.per) c.bounds.push_back(at);
+    c.bounds.push_back(extent);
+  }
+  if ((int64_t)c.bounds.size() - 1 > kPipeMaxChunks) {   // fall back to equal chunks within the limit
+    const int64_t per = (extent + kPipeMaxChunks - 1) / kPipeMaxChunks;
+    c.bounds.assign(1, 0);
+    for (int64_t at = per; at < extent; at += per) c.bounds.push_back(at);
+    c.bounds.push_back(extent);
+  }
   return c;
 }
 
 int run_pipelined(const Plan& l, const ModTables& T, const View& f, void* ws, const Dev& d, PipeRes* pr,
                   const Chunking& ch, cudaStream_t s, void* const* gev, int ngev, int* launches, double* out_host) {
-  const int64_t extent = ch.by_batch ? l.batch : l.M;
-  const int C = (int)((extent + ch.per - 1) / ch.per);
+  const int C = (int)ch.bounds.size() - 1;
   // GEMM units in launch order: the column blocks of row chunk 0, then row chunks 1.. (or member chunks).
   std::vector<View> rows(C), units;
   for (int c = 0; c < C; c++) {
-    const int64_t a0 = c * ch.per, a1 = std::min(extent, a0 + ch.per);
+    const int64_t a0 = ch.bounds[c], a1 = ch.bounds[c + 1];
     rows[c] = ch.by_batch ? batch_chunk(l, f, a0, a1) : row_chunk(l, f, a0, a1);
   }
   const int J = ch.cols > 0 ? (int)((l.N + ch.cols - 1) / ch.cols) : 1;

@@ -100,6 +100,8 @@ struct ReconArgs {
   double* C;             // [batch * M][N], row pitch ldc
   int64_t ldc;
 };
-void launch_reconstruct(const ReconArgs& a, const ModTables& T, cudaStream_t s);
+// beside_gemm: the launch runs beside a resident GEMM chunk (picks the form
+// that takes less from it).
+void launch_reconstruct(const ReconArgs& a, const ModTables& T, cudaStream_t s, bool beside_gemm = false);
 
 }  // namespace f64e

@@ -11,7 +11,9 @@
 // rounds the 128-bit value once to double, the fast mode combines in fp64 with
 // the reference's fused multiply-adds.  The result is scaled by
 // 2^-(sA_i + sB_j).
+#include <algorithm>
 #include <cstdlib>
+#include <cstring>
 
 #include "f64e_device.cuh"
 #include "f64e_kernels.h"
@@ -434,7 +436,8 @@ __global__ void __launch_bounds__(256, 4) reconstruct_crt_kernel(const ReconArgs
   }
 }
 
-void launch_reconstruct(const ReconArgs& a, const ModTables& T, cudaStream_t s) {
+
+void launch_reconstruct(const ReconArgs& a, const ModTables& T, cudaStream_t s, bool beside_gemm) {
   if (a.MF <= 0 || a.N <= 0) return;
   const int64_t nq = (a.N + 3) >> 2;
   const dim3 grid((unsigned)std::min<int64_t>((nq + 63) / 64, 1 << 20),
@@ -443,7 +446,11 @@ void launch_reconstruct(const ReconArgs& a, const ModTables& T, cudaStream_t s) 
   // F64E_RECON_GARNER=1 keeps exact products on the digit-by-digit kernels
   // (A/B checks of the direct CRT form); read per call.
   const char* gv = std::getenv("F64E_RECON_GARNER");
-  if (a.exact && T.crt_ok && !(gv && gv[0] == '1')) {
+  // The direct CRT kernel is the faster one alone (64 registers, four blocks
+  // per SM); beside a resident GEMM chunk the Garner kernel (112 registers: one
+  // block beside the GEMM CTA) takes less from the GEMM, and the product is
+  // faster with it there (measured on row-chunked 8192^3 products).
+  if (a.exact && T.crt_ok && !beside_gemm && !(gv && gv[0] == '1')) {
     switch (a.corr_mode) {
       case 0: reconstruct_crt_kernel<0><<<grid, block, 0, s>>>(a, T); break;
       case 1: reconstruct_crt_kernel<1><<<grid, block, 0, s>>>(a, T); break;

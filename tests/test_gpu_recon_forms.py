@@ -1,6 +1,7 @@
 """The two exact reconstruction forms must agree bit for bit: the direct CRT
-sum (default for modulus sets with M < 2^121) and the digit-by-digit balanced
-Garner form (F64E_RECON_GARNER=1).  Every correction layout (none, one fused
+sum (modulus sets with M < 2^121; chosen where the reconstruction runs alone)
+and the digit-by-digit balanced Garner form (chosen beside GEMM chunks;
+F64E_RECON_GARNER=1 forces it).  Every correction layout (none, one fused
 plane, two planes, deep-K int64 sums), several modulus counts, ragged shapes,
 batches and non-finite inputs; the CPU oracle pins one of each."""
 import os
@@ -24,6 +25,7 @@ def emu():
 
 
 def _both(fn):
+    """(Garner form, default form) of the same product."""
     old = os.environ.get("F64E_RECON_GARNER")
     try:
         os.environ["F64E_RECON_GARNER"] = "1"

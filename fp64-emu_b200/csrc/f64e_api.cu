@@ -138,7 +138,6 @@ int get_tables(const int32_t* primes, int P, ModTables* out) {
     T.kl[t] = kl;
     T.kh[t] = kh;
     T.mex[t] = (uint32_t)(((1ULL << 32) + p - 1) / p);
-    T.hh[t] = (uint32_t)(p / 2);
     if (p <= 128) T.fast_recon = 0;
     T.mrec[t] = (p > 128) ? (uint32_t)(((1ULL << 39) + p - 1) / p) : 0;
   }

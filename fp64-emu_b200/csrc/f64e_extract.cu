@@ -5,15 +5,21 @@
 // T = RNE(|x| * 2^s) is taken from the raw IEEE bits with integer arithmetic
 // only; the biased value T +- 2^b splits into three 18-bit limbs whose
 // weighted sum is reduced once per modulus with a 32-bit Barrett step to a
-// balanced residue; the two correction digits are hi = clamp(RNE(T*2^(7-b)))
-// and q = clamp(RNE(resid*2^8)).  The integer sequence (including its wrap on
-// non-finite rows) is the reference's, so the planes are bit-identical for
-// every input.
+// residue; the two correction digits are hi = clamp(RNE(T*2^(7-b))) and
+// q = clamp(RNE(resid*2^8)).  The integer sequence (including its wrap on
+// non-finite rows) is the reference's, so every plane holds, element by
+// element, the reference's residue modulo its p (and the correction planes
+// the reference's digits bit for bit).
 //
-// Layout differences from the reference: planes are K-major with a 16-byte
-// row pitch (TMA-legal for any K, pad columns zero), and an operand given as
-// [K, N] is transposed inside the extraction through shared memory instead of
-// by a separate fp64 transpose copy (fp64_emu.cu:1233-1235).
+// Differences from the reference: the residue byte of the common path is
+// ((v + 128) mod p) - 128, in [-128, p - 129], instead of the symmetric
+// balanced residue: the same value modulo p and within int8, one multiply
+// cheaper to form.  The GEMM needs only |residue| <= 128 (so that K terms of
+// at most 2^14 stay inside int32 for K < 2^17) and everything after it works
+// modulo p, so the products are bit-identical.  Planes are K-major with a
+// 16-byte row pitch (TMA-legal for any K, pad columns zero), and an operand
+// given as [K, N] is transposed inside the extraction through shared memory
+// instead of by a separate fp64 transpose copy (fp64_emu.cu:1233-1235).
 #include "f64e_device.cuh"
 #include "f64e_kernels.h"
 
@@ -124,14 +130,14 @@ __device__ __forceinline__ uint32_t residue_ref(uint64_t u, uint32_t p, uint32_t
   return (uint32_t)(uint8_t)(int8_t)rb;
 }
 
-// Fast form for u < 2^56: v = (u + cb) folded to under 2^19 by two dp4a over
-// the seven bytes of u; q = floor((v + h) / p) is the high word of
-// v * mex + h * mex exactly (v + h < 2^24); v - q p is the balanced residue.
-__device__ __forceinline__ uint32_t residue_fast(uint32_t lo, uint32_t hi, uint32_t kl, uint32_t kh, uint32_t cb,
-                                                 uint32_t mex, uint64_t hm, uint32_t p) {
-  const uint32_t v = __dp4a(lo, kl, __dp4a(hi, kh, cb));
-  const uint32_t q = (uint32_t)(((uint64_t)v * mex + hm) >> 32);
-  return v - q * p;
+// Fast form for u < 2^56: v = u + cb + 128 folded to under 2^20 by two dp4a
+// over the seven bytes of u (cb undoes the 2^b bias modulo p); r = v mod p is
+// v - umulhi(v, mex) p exactly (v < 2^24, p <= 256).  The caller stores
+// r - 128 = r ^ 0x80 per byte: congruent to u - 2^b, in [-128, p - 129].
+__device__ __forceinline__ uint32_t residue_fast(uint32_t lo, uint32_t hi, uint32_t kl, uint32_t kh, uint32_t cb128,
+                                                 uint32_t mex, uint32_t p) {
+  const uint32_t v = __dp4a(lo, kl, __dp4a(hi, kh, cb128));
+  return v - __umulhi(v, mex) * p;
 }
 
 __device__ __forceinline__ uint32_t pack4(uint32_t b0, uint32_t b1, uint32_t b2, uint32_t b3) {
@@ -146,18 +152,17 @@ template <int NE>
 __device__ __forceinline__ void residue_words(const Split (&S)[NE], const ModTables& T, int t, int be,
                                               uint32_t (&w)[NE / 4]) {
   const uint32_t p = T.p[t];
-  const uint32_t cb = p - (uint32_t)T.pow2mod[t][be - 16];
+  const uint32_t cb128 = p + 128u - (uint32_t)T.pow2mod[t][be - 16];
   const uint32_t kl = T.kl[t], kh = T.kh[t], mex = T.mex[t];
-  const uint64_t hm = (uint64_t)T.hh[t] * mex;
 #pragma unroll
   for (int i = 0; i < NE / 4; i++) {
     uint32_t r[4];
 #pragma unroll
     for (int e = 0; e < 4; e++) {
       const uint64_t u = S[4 * i + e].u;
-      r[e] = residue_fast((uint32_t)u, (uint32_t)(u >> 32), kl, kh, cb, mex, hm, p);
+      r[e] = residue_fast((uint32_t)u, (uint32_t)(u >> 32), kl, kh, cb128, mex, p);
     }
-    w[i] = pack4(r[0], r[1], r[2], r[3]);
+    w[i] = pack4(r[0], r[1], r[2], r[3]) ^ 0x80808080u;
   }
 }
 
@@ -172,6 +177,46 @@ __device__ __noinline__ uint32_t residue_word_ref(uint64_t u0, uint64_t u1, uint
 
 }  // namespace
 
+// Eight k-consecutive elements of one row of the operand (shift s; fast: the
+// row's maximum is finite and 2^s a normal double, p2s = 2^s): split, and
+// their 8 bytes written to every plane at dst + t * pstride.
+__device__ __forceinline__ void extract8(const double (&x)[8], int s, bool fast, double p2s, double p2h, int be,
+                                         bool corr, const ExtractArgs& a, const ModTables& T, int8_t* dst) {
+  const int P = T.P;
+  const int64_t pstride = a.pstride;
+  Split S[8];
+  bool ok = true;
+#pragma unroll
+  for (int u = 0; u < 8; u++) {
+    if (!(fast && split_fast(x[u], p2s, p2h, be, corr, S[u]))) S[u] = split_slow(x[u], s, be, corr);
+    ok = ok && (S[u].u >> 56) == 0;
+  }
+  // The reference form only for groups holding an element of a row with a
+  // non-finite maximum (u >= 2^56).
+  if (ok) {
+#pragma unroll
+    for (int t = 0; t < kMaxP; t++) {
+      if (t >= P) break;
+      uint32_t w[2];
+      residue_words<8>(S, T, t, be, w);
+      *reinterpret_cast<uint2*>(dst + t * pstride) = make_uint2(w[0], w[1]);
+    }
+  } else {
+    for (int t = 0; t < P; t++) {
+      const uint32_t p = T.p[t], cb = p - (uint32_t)T.pow2mod[t][be - 16];
+      *reinterpret_cast<uint2*>(dst + t * pstride) =
+          make_uint2(residue_word_ref(S[0].u, S[1].u, S[2].u, S[3].u, p, T.c36[t], T.c18[t], cb, T.mu2[t]),
+                     residue_word_ref(S[4].u, S[5].u, S[6].u, S[7].u, p, T.c36[t], T.c18[t], cb, T.mu2[t]));
+    }
+  }
+  if (corr) {
+    *reinterpret_cast<uint2*>(dst + a.hi_plane * pstride) =
+        make_uint2(pack4i(S[0].h, S[1].h, S[2].h, S[3].h), pack4i(S[4].h, S[5].h, S[6].h, S[7].h));
+    *reinterpret_cast<uint2*>(dst + a.q_plane * pstride) =
+        make_uint2(pack4i(S[0].q, S[1].q, S[2].q, S[3].q), pack4i(S[4].q, S[5].q, S[6].q, S[7].q));
+  }
+}
+
 // [rows, K] operand: thread (x, y) of a (32, 8) block handles 8 consecutive
 // columns of one row; a warp covers 256 columns (2 KB read, 256 B written per
 // plane, both contiguous).
@@ -183,9 +228,7 @@ __global__ void __launch_bounds__(256) extract_rows_kernel(const ExtractPair ap,
   const Gain gn = pick_gain(a.maxlg[0], a.maxlg[1], T.log2M, a.bits);
   const int be = gn.bits_eff;
   const bool corr = a.use_corr != 0;
-  const int P = T.P;
   const int64_t nch = a.Kp >> 3;
-  const int64_t pstride = a.pstride;
   for (int64_t r = (int64_t)blockIdx.y * 8 + threadIdx.y; r < a.rows; r += (int64_t)gridDim.y * 8) {
     const int s = (int)a.sft[r] + gn.g;
     const bool row_fast = (s >= -960) && (s <= 960);
@@ -206,147 +249,57 @@ __global__ void __launch_bounds__(256) extract_rows_kernel(const ExtractPair ap,
 #pragma unroll
         for (int u = 0; u < 8; u++) x[u] = (k0 + u < a.K) ? __ldg(xr + k0 + u) : 0.0;
       }
-      Split S[8];
-      bool ok = true;
-#pragma unroll
-      for (int u = 0; u < 8; u++) {
-        if (!(row_fast && split_fast(x[u], p2s, p2h, be, corr, S[u]))) S[u] = split_slow(x[u], s, be, corr);
-        ok = ok && (S[u].u >> 56) == 0;
-      }
-      // The reference form only for chunks holding an element of a row with a
-      // non-finite maximum (u >= 2^56).
-      int8_t* dst = a.planes + r * a.Kp + k0;
-      if (ok) {
-#pragma unroll
-        for (int t = 0; t < kMaxP; t++) {
-          if (t >= P) break;
-          uint32_t w[2];
-          residue_words<8>(S, T, t, be, w);
-          *reinterpret_cast<uint2*>(dst + t * pstride) = make_uint2(w[0], w[1]);
-        }
-      } else {
-        for (int t = 0; t < P; t++) {
-          const uint32_t p = T.p[t], cb = p - (uint32_t)T.pow2mod[t][be - 16];
-          *reinterpret_cast<uint2*>(dst + t * pstride) =
-              make_uint2(residue_word_ref(S[0].u, S[1].u, S[2].u, S[3].u, p, T.c36[t], T.c18[t], cb, T.mu2[t]),
-                         residue_word_ref(S[4].u, S[5].u, S[6].u, S[7].u, p, T.c36[t], T.c18[t], cb, T.mu2[t]));
-        }
-      }
-      if (corr) {
-        *reinterpret_cast<uint2*>(dst + a.hi_plane * pstride) =
-            make_uint2(pack4i(S[0].h, S[1].h, S[2].h, S[3].h), pack4i(S[4].h, S[5].h, S[6].h, S[7].h));
-        *reinterpret_cast<uint2*>(dst + a.q_plane * pstride) =
-            make_uint2(pack4i(S[0].q, S[1].q, S[2].q, S[3].q), pack4i(S[4].q, S[5].q, S[6].q, S[7].q));
-      }
+      extract8(x, s, row_fast, p2s, p2h, be, corr, a, T, a.planes + r * a.Kp + k0);
     }
   }
 }
 
-// [batch, K, N] operand: a block transposes a 64 (k) x 32 (n) tile.  Thread
-// (n = lane, warp w) reads columns coalesced along n for the k quads w and
-// w + 8 and splits its eight elements once; then, for each group of up to 11
-// planes, it packs four k-consecutive residues per plane into one word in
-// shared memory (row pitch 17 words: conflict-free writes) and the block
-// writes each plane's 32 x 64-byte tile as 16-byte vectors along K.  Two
-// plane groups keep the block at 24 KB of shared memory, so it runs beside a
-// resident GEMM CTA.
-constexpr int kColTileK = 64, kColTileN = 32, kColPitch = 17, kColGroup = 11;
-static_assert(2 * kColGroup >= kMaxP + 2, "two plane groups cover every plane");
+// [batch, K, N] operand: a block takes a 64 (k) x 32 (n) tile.  Warp w reads
+// the rows k0 + w + 8 i (32 consecutive n, 256 B each) and parks the doubles
+// transposed in shared memory, 66 per n (16.5 KB); thread (n, kg) then splits
+// the eight k-consecutive elements kg of its n exactly as extract_rows does
+// and writes 8 bytes per plane.  A warp takes 8 n x 4 k-groups: each plane
+// store is 32 contiguous bytes in each of 8 plane rows, and each 8-lane phase
+// of its 16-byte shared loads reads 8 different n, whose pitch of 33 16-byte
+// chunks puts them in 8 different bank groups.
+constexpr int kColTileK = 64, kColTileN = 32, kColPitch = 66;
 
-template <int T0>
-__device__ __forceinline__ void cols_fill_group(uint32_t (*sw)[kColTileN][kColPitch], const Split (&S)[2][4],
-                                                const bool (&ok)[2], const ExtractArgs& a, const ModTables& T,
-                                                int be, bool corr, int tx, int ty) {
-  const int P = T.P;
-#pragma unroll
-  for (int qi = 0; qi < 2; qi++) {
-    const int qd = ty + 8 * qi;
-    if (ok[qi]) {
-#pragma unroll
-      for (int tt = 0; tt < kColGroup; tt++) {
-        const int t = T0 + tt;
-        if (t >= P || t >= kMaxP) break;
-        uint32_t w[1];
-        residue_words<4>(S[qi], T, t, be, w);
-        sw[tt][tx][qd] = w[0];
-      }
-    } else {
-      for (int t = T0; t < min(P, T0 + kColGroup); t++) {
-        const uint32_t p = T.p[t], cb = p - (uint32_t)T.pow2mod[t][be - 16];
-        sw[t - T0][tx][qd] = residue_word_ref(S[qi][0].u, S[qi][1].u, S[qi][2].u, S[qi][3].u, p, T.c36[t], T.c18[t],
-                                              cb, T.mu2[t]);
-      }
-    }
-    if (corr) {
-      if (a.hi_plane >= T0 && a.hi_plane < T0 + kColGroup)
-        sw[a.hi_plane - T0][tx][qd] = pack4i(S[qi][0].h, S[qi][1].h, S[qi][2].h, S[qi][3].h);
-      if (a.q_plane >= T0 && a.q_plane < T0 + kColGroup)
-        sw[a.q_plane - T0][tx][qd] = pack4i(S[qi][0].q, S[qi][1].q, S[qi][2].q, S[qi][3].q);
-    }
-  }
-}
-
-__device__ __forceinline__ void cols_write_group(uint32_t (*sw)[kColTileN][kColPitch], const ExtractArgs& a, int t0,
-                                                 int nt, int64_t b, int64_t n0, int64_t k0) {
-  for (int i = threadIdx.x; i < nt * 128; i += 256) {
-    const int tt = i >> 7, rem = i & 127, row = rem >> 2, part = rem & 3;
-    const int64_t nn = n0 + row, kk = k0 + part * 16;
-    if (nn < a.N && kk < a.Kp) {
-      const uint4 v = make_uint4(sw[tt][row][part * 4 + 0], sw[tt][row][part * 4 + 1], sw[tt][row][part * 4 + 2],
-                                 sw[tt][row][part * 4 + 3]);
-      *reinterpret_cast<uint4*>(a.planes + (t0 + tt) * a.pstride + (b * a.N + nn) * a.Kp + kk) = v;
-    }
-  }
-}
-
-// Four blocks per SM (64 registers): the transposing kernel is latency-bound
-// and gains more from occupancy than it loses to the tighter register budget.
-__global__ void __launch_bounds__(256, 4) extract_cols_kernel(const ExtractArgs a, const ModTables T) {
-  __shared__ uint32_t sw[kColGroup][kColTileN][kColPitch];
-  const Gain gn = pick_gain(a.maxlg[0], a.maxlg[1], T.log2M, a.bits);
-  const int be = gn.bits_eff;
-  const bool corr = a.use_corr != 0;
+__global__ void __launch_bounds__(256, 2) extract_cols_kernel(const ExtractArgs a, const ModTables T) {
+  __shared__ __align__(16) double xs[kColTileN * kColPitch];
   const int64_t b = blockIdx.z;
   const int64_t n0 = (int64_t)blockIdx.x * kColTileN, k0 = (int64_t)blockIdx.y * kColTileK;
-  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
-  const int64_t n = n0 + tx;
-  const bool nin = n < a.N;
-  const int s = nin ? (int)a.sft[b * a.N + n] + gn.g : 0;
-  const bool col_fast = (s >= -960) && (s <= 960);
-  const double p2s = pow2d(col_fast ? s : 0), p2h = pow2d(7 - be);
-  const double* __restrict__ xb = a.X + b * a.K * a.ld + n;   // row pitch a.ld (>= a.N)
-  // all eight loads first (the out-of-line slow split would otherwise hold
-  // the second quad's loads back until the first quad is split)
-  double x[2][4];
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  {
+    const int64_t n = n0 + lane;
+    const bool nin = n < a.N;
+    const double* __restrict__ xb = a.X + b * a.K * a.ld + n;   // row pitch a.ld (>= a.N)
+    double v[8];
 #pragma unroll
-  for (int qi = 0; qi < 2; qi++)
-#pragma unroll
-    for (int u = 0; u < 4; u++) {
-      const int64_t k = k0 + 4 * (ty + 8 * qi) + u;
-      x[qi][u] = (nin && k < a.K) ? __ldg(xb + k * a.ld) : 0.0;
+    for (int i = 0; i < 8; i++) {
+      const int64_t k = k0 + w + 8 * i;
+      v[i] = (nin && k < a.K) ? __ldg(xb + k * a.ld) : 0.0;
     }
-  Split S[2][4];
-  bool ok[2];
 #pragma unroll
-  for (int qi = 0; qi < 2; qi++) {
-    ok[qi] = true;
-#pragma unroll
-    for (int u = 0; u < 4; u++) {
-      if (!(col_fast && split_fast(x[qi][u], p2s, p2h, be, corr, S[qi][u])))
-        S[qi][u] = split_slow(x[qi][u], s, be, corr);
-      ok[qi] = ok[qi] && (S[qi][u].u >> 56) == 0;
-    }
+    for (int i = 0; i < 8; i++) xs[lane * kColPitch + w + 8 * i] = v[i];
   }
-  const int G = T.P + (corr ? 2 : 0);
-  cols_fill_group<0>(sw, S, ok, a, T, be, corr, tx, ty);
   __syncthreads();
-  cols_write_group(sw, a, 0, min(G, kColGroup), b, n0, k0);
-  if (G > kColGroup) {
-    __syncthreads();
-    cols_fill_group<kColGroup>(sw, S, ok, a, T, be, corr, tx, ty);
-    __syncthreads();
-    cols_write_group(sw, a, kColGroup, G - kColGroup, b, n0, k0);
+  const int nl = 8 * (w & 3) + (lane & 7), kg = 4 * (w >> 2) + (lane >> 3);
+  const int64_t n = n0 + nl, kk = k0 + 8 * kg;
+  if (n >= a.N || kk >= a.Kp) return;
+  double x[8];
+  const double2* src = reinterpret_cast<const double2*>(xs + nl * kColPitch + 8 * kg);
+#pragma unroll
+  for (int u = 0; u < 4; u++) {
+    const double2 d = src[u];
+    x[2 * u] = d.x;
+    x[2 * u + 1] = d.y;
   }
+  const Gain gn = pick_gain(a.maxlg[0], a.maxlg[1], T.log2M, a.bits);
+  const int be = gn.bits_eff;
+  const int s = (int)a.sft[b * a.N + n] + gn.g;
+  const bool fast = (s >= -960) && (s <= 960);
+  extract8(x, s, fast, pow2d(fast ? s : 0), pow2d(7 - be), be, a.use_corr != 0, a, T,
+           a.planes + (b * a.N + n) * a.Kp + kk);
 }
 
 namespace {

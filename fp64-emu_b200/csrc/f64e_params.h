@@ -28,12 +28,10 @@ struct ModTables {
   // Fast forms (exact quotients, no correction steps).  Extraction: the
   // residue pre-sum of a biased integer u < 2^56 is two dp4a over its seven
   // bytes with the weights 2^(8i) mod p; its quotient by p is umulhi(v, mex)
-  // exactly for v < 2^24.  The balanced residue is ((v + h) mod p) - h with
-  // h = floor(p / 2).
+  // exactly for v < 2^24.  The stored residue is ((v + 128) mod p) - 128.
   uint32_t kl[kMaxP];          // bytes 2^0, 2^8, 2^16, 2^24 mod p
   uint32_t kh[kMaxP];          // bytes 2^32, 2^40, 2^48 mod p (top byte 0)
   uint32_t mex[kMaxP];         // ceil(2^32 / p)
-  uint32_t hh[kMaxP];          // floor(p / 2)
   // Reconstruction with digits stored offset, d' = d + h in [0, p): the
   // Garner sum uses unsigned factors cu = M_u mod p_t, and the offset terms
   // fold into one constant per digit, krec = ((sum_u h_u cu) * minv + h_t)

@@ -184,9 +184,23 @@ __device__ __noinline__ uint32_t residue_word_ref(uint64_t u0, uint64_t u1, uint
 
 }  // namespace
 
+__device__ __forceinline__ void store_corr(const Split (&S)[8], bool corr, const ExtractArgs& a, int8_t* dst) {
+  if (corr) {
+    *reinterpret_cast<uint2*>(dst + a.hi_plane * a.pstride) =
+        make_uint2(pack4i(S[0].h, S[1].h, S[2].h, S[3].h), pack4i(S[4].h, S[5].h, S[6].h, S[7].h));
+    *reinterpret_cast<uint2*>(dst + a.q_plane * a.pstride) =
+        make_uint2(pack4i(S[0].q, S[1].q, S[2].q, S[3].q), pack4i(S[4].q, S[5].q, S[6].q, S[7].q));
+  }
+}
+
 // Eight k-consecutive elements of one row of the operand (shift s; fast: the
 // row's maximum is finite and 2^s a normal double, p2s = 2^s): split, and
-// their 8 bytes written to every plane at dst + t * pstride.
+// their 8 bytes written to every plane at dst + t * pstride.  CORR_FIRST
+// stores the two correction planes before the residues, which frees their
+// registers for the residue loop (64 registers in extract_cols: four blocks
+// per SM).  The row kernel keeps them last: beside a resident GEMM chunk its
+// measured products were faster that way.
+template <bool CORR_FIRST>
 __device__ __forceinline__ void extract8(const double (&x)[8], int s, bool fast, double p2s, double p2h, int be,
                                          bool corr, const ExtractArgs& a, const ModTables& T, int8_t* dst) {
   const int P = T.P;
@@ -199,6 +213,7 @@ __device__ __forceinline__ void extract8(const double (&x)[8], int s, bool fast,
     if (!(fast && split_fast(x[u], p2s, p2h, bias, corr, S[u]))) S[u] = split_slow(x[u], s, be, corr);
     top |= (uint32_t)(S[u].u >> 32);
   }
+  if (CORR_FIRST) store_corr(S, corr, a, dst);
   // The reference form only for groups holding an element of a row with a
   // non-finite maximum (u >= 2^56).
   if ((top >> 24) == 0) {
@@ -217,12 +232,7 @@ __device__ __forceinline__ void extract8(const double (&x)[8], int s, bool fast,
                      residue_word_ref(S[4].u, S[5].u, S[6].u, S[7].u, p, T.c36[t], T.c18[t], cb, T.mu2[t]));
     }
   }
-  if (corr) {
-    *reinterpret_cast<uint2*>(dst + a.hi_plane * pstride) =
-        make_uint2(pack4i(S[0].h, S[1].h, S[2].h, S[3].h), pack4i(S[4].h, S[5].h, S[6].h, S[7].h));
-    *reinterpret_cast<uint2*>(dst + a.q_plane * pstride) =
-        make_uint2(pack4i(S[0].q, S[1].q, S[2].q, S[3].q), pack4i(S[4].q, S[5].q, S[6].q, S[7].q));
-  }
+  if (!CORR_FIRST) store_corr(S, corr, a, dst);
 }
 
 // [rows, K] operand: thread (x, y) of a (32, 8) block handles 8 consecutive
@@ -260,7 +270,7 @@ __global__ void __launch_bounds__(256, 3) extract_rows_kernel(const ExtractPair 
 #pragma unroll
         for (int u = 0; u < 8; u++) x[u] = (k0 + u < a.K) ? __ldg(xr + k0 + u) : 0.0;
       }
-      extract8(x, s, row_fast, p2s, p2h, be, corr, a, T, a.planes + r * a.Kp + k0);
+      extract8<false>(x, s, row_fast, p2s, p2h, be, corr, a, T, a.planes + r * a.Kp + k0);
     }
   }
 }
@@ -309,7 +319,7 @@ __global__ void __launch_bounds__(256, 2) extract_cols_kernel(const ExtractArgs 
   const int be = gn.bits_eff;
   const int s = (int)a.sft[b * a.N + n] + gn.g;
   const bool fast = (s >= -960) && (s <= 960);
-  extract8(x, s, fast, pow2d(fast ? s : 0), pow2d(7 - be), be, a.use_corr != 0, a, T,
+  extract8<true>(x, s, fast, pow2d(fast ? s : 0), pow2d(7 - be), be, a.use_corr != 0, a, T,
            a.planes + (b * a.N + n) * a.Kp + kk);
 }
 

@@ -15,6 +15,9 @@ the two sizing maxima; total work is fixed, so scaling is "strong".
           memory and the product copied back inside the timed region
   roofline  the modular tensor-core GEMM (the dominant kernel): INT8 ops
           per launch / its average duration over the timed region
+  accuracy  the metric's "correct bits vs dd": after timing, the product's
+          first 256 rows (rank 0's block) against a double-double product,
+          with cuBLAS DGEMM on the same sample (fp64_emu.accuracy)
 
 --impl reference runs the reference's own CUDA kernels (the build in
 oracle/_ref, compiled from the reference sources; the reference has no CPU
@@ -482,8 +485,39 @@ def run_ours(args):
             result["cpu_fp64_torch"] = {"value": None, "error": str(e)[:200]}
     if rank == 0 and not args.no_native:
         result["native_dgemm"] = native_dgemm(A_l, B_l, nt, args)
+    if rank == 0 and not args.no_accuracy:
+        try:
+            result["accuracy"] = accuracy_sample(kind, A_l, B_l, step.out,
+                                                 others={"native_dgemm": lambda a, b: a @ b})
+        except Exception as e:  # noqa: BLE001
+            result["accuracy"] = {"error": str(e)[:200]}
     if rank == 0:
         print(json.dumps(result), flush=True)
+
+
+def accuracy_sample(kind, A, B, C, others=None, rows=256):
+    """Correct bits against the double-double product (fp64_emu.accuracy)
+    on a sample: the first `rows` rows of the block (of batch member 0) by
+    every column.  `others`: name -> callable giving another product of the
+    same sample to measure alongside (cuBLAS DGEMM).  Runs after timing."""
+    from fp64_emu import accuracy as acc
+    nt = kind in ("mm_nt", "bmm_nt")
+    batched = A.dim() == 3
+    if batched:
+        A, B, C = A[0], B[0], C[0]
+    R = min(rows, A.size(0))
+    As = A[:R]
+    Bt = (B if nt else B.t()).contiguous()
+    t0 = time.perf_counter()
+    hi, lo = acc.dd_product(As, Bt)
+    res = {"sample": f"{R} rows x {Bt.size(1)} columns" + (" of batch member 0" if batched else ""),
+           "measure": "-log2(max|C - hi - lo| / max|hi|) against the double-double product (hi, lo); "
+                      "element bits: -log2(|C - hi - lo| / |hi|), capped at 60",
+           "value": acc.summary(C[:R], hi, lo)}
+    for name, fn in (others or {}).items():
+        res[name] = acc.summary(fn(As, Bt), hi, lo)
+    res["seconds"] = round(time.perf_counter() - t0, 1)
+    return res
 
 
 def native_dgemm(A, B, nt, args):
@@ -585,6 +619,11 @@ def run_reference(args):
                                    "one B200: the reference has no CPU implementation of this path"},
         "clocks": clk,
     }
+    if not args.no_accuracy:
+        try:
+            result["accuracy"] = accuracy_sample(kind, A, B, C0)
+        except Exception as e:  # noqa: BLE001
+            result["accuracy"] = {"error": str(e)[:200]}
     print(json.dumps(result), flush=True)
 
 
@@ -599,6 +638,8 @@ def main():
     ap.add_argument("--cpu-rows", type=int, default=1024)
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baselines")
     ap.add_argument("--no-native", action="store_true", help="skip the cuBLAS DGEMM context number")
+    ap.add_argument("--no-accuracy", action="store_true",
+                    help="skip the correct-bits measurement after timing (one small launch per K step)")
     args = ap.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", "0"))

@@ -636,6 +636,7 @@ struct Chunking {
   bool by_batch = false;
   int64_t per = 0;    // rows (or members) per chunk; 0 = unchunked
   int64_t cols = 0;   // columns per block of the first row chunk; 0 = whole
+  int head = 1;       // row chunks of A extracted before the first GEMM (single products)
   std::vector<int64_t> bounds;   // chunk boundaries 0 = b_0 < b_1 < ... < b_C = extent
 };
 
@@ -669,6 +670,11 @@ Chunking pipe_chunking(const Plan& l) {
     if (c.cols > 0) c.cols = std::max<int64_t>(c.cols, (l.N + kPipeMaxCols - 1) / kPipeMaxCols);
     if (c.cols > 0) c.cols = round_up(c.cols, 16);
     if (c.cols >= l.N) c.cols = 0;
+  }
+  // Row chunks of A extracted in the head: F64E_PIPE_HEAD = n (0: all of A).
+  if (!c.by_batch) {
+    const int64_t hv = env_int("F64E_PIPE_HEAD");
+    if (hv >= 0) c.head = hv == 0 ? kPipeMaxChunks : (int)std::min<int64_t>(hv, kPipeMaxChunks);
   }
   // Boundaries.  Single products of at least three chunks start and end with
   // half-size chunks (the first one's extraction and the last one's
@@ -733,8 +739,10 @@ int run_pipelined(const Plan& l, const ModTables& T, const View& f, void* ws, co
   std::lock_guard<std::mutex> lk(pr->mtx);
   cudaEvent_t* E = pr->ev;
   int ne = 1;   // E[0] = fork
-  // Head, on the caller's stream: everything the first GEMM unit reads.
-  extract_A(l, T, rows[0], ws, 0, l.K, s);
+  // Head, on the caller's stream: everything the first GEMM unit reads (and
+  // the first H row chunks of A).
+  const int H = (ch.by_batch || J > 1) ? 1 : std::max(1, std::min(C, ch.head));
+  for (int c = 0; c < H; c++) extract_A(l, T, rows[c], ws, 0, l.K, s);
   if (ch.by_batch) extract_B(l, T, rows[0], ws, 0, l.K, s);
   else extract_B(l, T, J > 1 ? bcols[0] : f, ws, 0, l.K, s);
   cudaError_t e = cudaEventRecord(E[0], s);
@@ -747,7 +755,7 @@ int run_pipelined(const Plan& l, const ModTables& T, const View& f, void* ws, co
     cudaEventRecord(E[ne], pr->aux);
     need[j] = ne++;
   }
-  for (int c = 1; c < C; c++) {
+  for (int c = H; c < C; c++) {
     extract_A(l, T, rows[c], ws, 0, l.K, pr->aux);
     if (ch.by_batch) extract_B(l, T, rows[c], ws, 0, l.K, pr->aux);
     cudaEventRecord(E[ne], pr->aux);

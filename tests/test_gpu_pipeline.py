@@ -159,3 +159,67 @@ def test_chunked_product_in_a_cuda_graph(emu):
     torch.cuda.synchronize()
     assert torch.equal(got, want)
     assert torch.equal(got, flat)
+
+
+class envset:
+    """Set arbitrary environment switches for the duration of a block."""
+
+    def __init__(self, **kv):
+        self.kv = kv
+
+    def __enter__(self):
+        self.old = {k: os.environ.get(k) for k in self.kv}
+        for k, v in self.kv.items():
+            if v is None:
+                os.environ.pop(k, None)
+            else:
+                os.environ[k] = str(v)
+
+    def __exit__(self, *a):
+        for k, v in self.old.items():
+            if v is None:
+                os.environ.pop(k, None)
+            else:
+                os.environ[k] = v
+
+
+@pytest.mark.parametrize("head", [0, 2, 3])
+def test_head_depth_same_bits(emu, head):
+    # A chunks extracted before the first GEMM (F64E_PIPE_HEAD): 0 = all, n = n chunks;
+    # 6144 rows = chunks of 1024, 2048, 2048, 1024 with the half-size ends
+    g = torch.Generator(device="cuda").manual_seed(31)
+    A = torch.randn(6144, 700, dtype=torch.float64, device="cuda", generator=g)
+    Bt = torch.randn(700, 900, dtype=torch.float64, device="cuda", generator=g)
+    with envset(F64E_PIPE_HEAD=None):
+        want = emu.mm_nt(A, Bt)
+    with envset(F64E_PIPE_HEAD=head):
+        got = emu.mm_nt(A, Bt)
+    torch.cuda.synchronize()
+    assert torch.equal(got, want)
+
+
+@pytest.mark.parametrize("ends", [0, 1])
+def test_equal_or_half_ends_same_bits(emu, ends):
+    g = torch.Generator(device="cuda").manual_seed(32)
+    A = torch.randn(8192, 300, dtype=torch.float64, device="cuda", generator=g)   # 4 x 2048 or 1024, 3 x 2048, 1024
+    B = torch.randn(500, 300, dtype=torch.float64, device="cuda", generator=g)
+    with envset(F64E_PIPE_CHUNK=0):
+        want = emu.mm(A, B)
+    with envset(F64E_PIPE_ENDS=ends):
+        got = emu.mm(A, B)
+    torch.cuda.synchronize()
+    assert torch.equal(got, want)
+
+
+def test_single_cta_gemm_same_bits(emu):
+    # F64E_GEMM_SINGLE=1: every product on the one-CTA GEMM instead of the CTA pair
+    g = torch.Generator(device="cuda").manual_seed(33)
+    for (M, K, N) in [(600, 1000, 520), (2304, 512, 700)]:
+        A = torch.randn(M, K, dtype=torch.float64, device="cuda", generator=g)
+        Bt = torch.randn(K, N, dtype=torch.float64, device="cuda", generator=g)
+        with envset(F64E_GEMM_SINGLE=None):
+            want = emu.mm_nt(A, Bt)
+        with envset(F64E_GEMM_SINGLE=1):
+            got = emu.mm_nt(A, Bt)
+        torch.cuda.synchronize()
+        assert torch.equal(got, want)

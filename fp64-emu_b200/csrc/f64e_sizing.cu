@@ -152,17 +152,16 @@ __global__ void __launch_bounds__(256) col_partial_kernel(const double* __restri
   const double* __restrict__ base = X + b * K * N + n;
   double mx = 0.0, ss = 0.0;
   int64_t k = k0;
-  for (; k + 3 < k1; k += 4) {
-    const double v0 = __ldg(base + k * N), v1 = __ldg(base + (k + 1) * N), v2 = __ldg(base + (k + 2) * N),
-                 v3 = __ldg(base + (k + 3) * N);
-    mx = fmax(mx, fabs(v0));
-    ss = fma(v0, v0, ss);
-    mx = fmax(mx, fabs(v1));
-    ss = fma(v1, v1, ss);
-    mx = fmax(mx, fabs(v2));
-    ss = fma(v2, v2, ss);
-    mx = fmax(mx, fabs(v3));
-    ss = fma(v3, v3, ss);
+  // eight loads in flight, accumulated in k order
+  for (; k + 7 < k1; k += 8) {
+    double v[8];
+#pragma unroll
+    for (int u = 0; u < 8; u++) v[u] = __ldg(base + (k + u) * N);
+#pragma unroll
+    for (int u = 0; u < 8; u++) {
+      mx = fmax(mx, fabs(v[u]));
+      ss = fma(v[u], v[u], ss);
+    }
   }
   for (; k < k1; k++) {
     const double v = __ldg(base + k * N);
@@ -174,20 +173,36 @@ __global__ void __launch_bounds__(256) col_partial_kernel(const double* __restri
 }
 
 // Column finalize of B plus the operand maxima by the last CTA to finish.
+// One warp per column: lane l loads the partials of slabs l, l + 32, ...,
+// and the warp adds them in slab order s = 0, 1, ... from shuffles (every
+// lane runs the same chain; lane 0 writes).  Narrow operands have up to 128
+// slabs, which a thread per column would walk one dependent load at a time.
 __global__ void __launch_bounds__(256) col_finalize_maxlg_kernel(const double* __restrict__ pmax,
                                                                  const double* __restrict__ pss, int64_t totalcols,
                                                                  int nslab, int bits, int16_t* __restrict__ sft,
                                                                  float* __restrict__ lg, const float* lgA,
                                                                  int64_t ra, float* __restrict__ maxlg,
                                                                  unsigned* __restrict__ counter) {
-  const int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int lane = threadIdx.x & 31;
+  const int64_t j = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
   if (j < totalcols) {
     double mx = 0.0, ss = 0.0;
-    for (int s = 0; s < nslab; s++) {
-      mx = fmax(mx, pmax[(int64_t)s * totalcols + j]);
-      ss += pss[(int64_t)s * totalcols + j];
+    for (int s0 = 0; s0 < nslab; s0 += 32) {
+      const int s = s0 + lane;
+      const double pm = s < nslab ? __ldcg(pmax + (int64_t)s * totalcols + j) : 0.0;
+      const double ps = s < nslab ? __ldcg(pss + (int64_t)s * totalcols + j) : 0.0;
+      const int n = min(32, nslab - s0);
+#pragma unroll
+      for (int u = 0; u < 32; u++) {
+        const double a = __shfl_sync(0xFFFFFFFFu, pm, u);
+        const double b = __shfl_sync(0xFFFFFFFFu, ps, u);
+        if (u < n) {
+          mx = fmax(mx, a);
+          ss += b;
+        }
+      }
     }
-    finish_stats(mx, ss, bits, &sft[j], &lg[j]);
+    if (lane == 0) finish_stats(mx, ss, bits, &sft[j], &lg[j]);
   }
   if (last_block_done(counter)) maxlg_block(lgA, ra, lg, totalcols, maxlg);
 }
@@ -219,7 +234,8 @@ void launch_col_stats_maxlg(const double* X, int64_t batch, int64_t K, int64_t N
   const int64_t NF = batch * N;
   const unsigned gx = (unsigned)std::max<int64_t>(1, (NF + 255) / 256);
   if (nslab > 0 && NF > 0) col_partial_kernel<<<dim3(gx, nslab), 256, 0, s>>>(X, NF, K, N, kslab, pmax, pss);
-  col_finalize_maxlg_kernel<<<gx, 256, 0, s>>>(pmax, pss, NF, nslab, bits, sft, lg, lgA, ra, maxlg, counter);
+  const unsigned gf = (unsigned)std::max<int64_t>(1, (NF + 7) / 8);   // a warp per column
+  col_finalize_maxlg_kernel<<<gf, 256, 0, s>>>(pmax, pss, NF, nslab, bits, sft, lg, lgA, ra, maxlg, counter);
 }
 
 }  // namespace f64e

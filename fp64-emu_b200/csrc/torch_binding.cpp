@@ -270,6 +270,58 @@ void gemm_host(at::Tensor& out, const at::Tensor& A, const at::Tensor& B, const 
   TORCH_CHECK(e == cudaSuccess, "fp64_emu: ", cudaGetErrorString(e));
 }
 
+// One product of fp64_emu.HostStream, queued without a host wait: the
+// operand copies on streams[0], the product on streams[1], the result copy on
+// streams[2] (raw cudaStream_t handles of the slot's device).  events (raw
+// cudaEvent_t, created): [caller, loaded, computed, done]; the three streams
+// first wait for what the caller's current stream queued before the call,
+// and when the slot held an earlier product (used) the copies into its
+// device operands wait until that product has read them and the product
+// waits until its result has left the device.
+void host_submit(at::Tensor& out, const at::Tensor& A, const at::Tensor& B, at::Tensor& Ad, at::Tensor& Bd,
+                 at::Tensor& Cd, at::Tensor& ws, const at::Tensor& primes_cpu, bool b_kn, bool exact, int64_t bits,
+                 bool use_corr, at::IntArrayRef streams, at::IntArrayRef events, bool used) {
+  TORCH_CHECK(!A.is_cuda() && !B.is_cuda() && !out.is_cuda(), "host submit: A, B and out must be CPU tensors");
+  TORCH_CHECK(Ad.is_cuda() && Bd.is_cuda() && Cd.is_cuda() && ws.is_cuda(), "host submit: device buffers");
+  TORCH_CHECK(Bd.device() == Ad.device() && Cd.device() == Ad.device() && ws.device() == Ad.device(),
+              "host submit: device buffers on one device");
+  for (const at::Tensor* t : std::initializer_list<const at::Tensor*>{&out, &A, &B, &Ad, &Bd, &Cd})
+    TORCH_CHECK(t->dtype() == at::kDouble && t->is_contiguous(), "host submit: contiguous f64 tensors");
+  TORCH_CHECK(A.sizes() == Ad.sizes() && B.sizes() == Bd.sizes() && out.sizes() == Cd.sizes(),
+              "host submit: host and device shapes differ");
+  TORCH_CHECK(ws.is_contiguous(), "host submit: contiguous workspace");
+  TORCH_CHECK(streams.size() == 3 && events.size() == 4, "host submit: 3 streams and 4 events");
+  for (const int64_t e : events) TORCH_CHECK(e != 0, "events must be created (record them once first)");
+  TORCH_CHECK(bits >= 16 && bits <= 53, "bits must be in [16, 53]");
+  const auto pr = host_primes(primes_cpu);
+  const f64e_problem p = problem_of(Ad, Bd, b_kn, pr, exact, bits, use_corr);
+  const c10::cuda::CUDAGuard guard(Ad.device());
+  cudaStream_t h2d = reinterpret_cast<cudaStream_t>(streams[0]), comp = reinterpret_cast<cudaStream_t>(streams[1]),
+               d2h = reinterpret_cast<cudaStream_t>(streams[2]);
+  cudaEvent_t caller = reinterpret_cast<cudaEvent_t>(events[0]), loaded = reinterpret_cast<cudaEvent_t>(events[1]),
+              computed = reinterpret_cast<cudaEvent_t>(events[2]), done = reinterpret_cast<cudaEvent_t>(events[3]);
+  cudaError_t e = cudaEventRecord(caller, static_cast<cudaStream_t>(stream_of()));
+  for (cudaStream_t st : {h2d, comp, d2h})
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(st, caller, 0);
+  if (used && e == cudaSuccess) e = cudaStreamWaitEvent(h2d, computed, 0);
+  if (used && e == cudaSuccess) e = cudaStreamWaitEvent(comp, done, 0);
+  if (e == cudaSuccess)
+    e = cudaMemcpyAsync(Ad.data_ptr(), A.data_ptr(), (size_t)A.numel() * 8, cudaMemcpyHostToDevice, h2d);
+  if (e == cudaSuccess)
+    e = cudaMemcpyAsync(Bd.data_ptr(), B.data_ptr(), (size_t)B.numel() * 8, cudaMemcpyHostToDevice, h2d);
+  if (e == cudaSuccess) e = cudaEventRecord(loaded, h2d);
+  if (e == cudaSuccess) e = cudaStreamWaitEvent(comp, loaded, 0);
+  TORCH_CHECK(e == cudaSuccess, "fp64_emu: ", cudaGetErrorString(e));
+  check(f64e_gemm(&p, Ad.data_ptr<double>(), Bd.data_ptr<double>(), Cd.data_ptr<double>(), ws.data_ptr(),
+                  (size_t)ws.numel() * ws.element_size(), comp, F64E_PHASE_ALL));
+  e = cudaEventRecord(computed, comp);
+  if (e == cudaSuccess) e = cudaStreamWaitEvent(d2h, computed, 0);
+  if (e == cudaSuccess)
+    e = cudaMemcpyAsync(out.data_ptr(), Cd.data_ptr(), (size_t)out.numel() * 8, cudaMemcpyDeviceToHost, d2h);
+  if (e == cudaSuccess) e = cudaEventRecord(done, d2h);
+  TORCH_CHECK(e == cudaSuccess, "fp64_emu: ", cudaGetErrorString(e));
+}
+
 void gemm_checked(at::Tensor& out, at::Tensor& ws, const at::Tensor& A, const at::Tensor& B,
                   const at::Tensor& primes_cpu, bool b_kn, bool exact, int64_t bits, bool use_corr) {
   gemm_phase(out, ws, A, B, primes_cpu, b_kn, exact, bits, use_corr, F64E_PHASE_ALL, true, 0);
@@ -329,6 +381,10 @@ TORCH_LIBRARY(fp64_emu_b200, ops) {
       "fp64_emu_gemm_host(Tensor! out, Tensor A, Tensor B, Tensor primes_cpu, bool b_kn, bool exact, int bits, "
       "bool use_corr) -> ()");
   ops.def(
+      "fp64_emu_host_submit(Tensor! out, Tensor A, Tensor B, Tensor! Ad, Tensor! Bd, Tensor! Cd, Tensor! ws, "
+      "Tensor primes_cpu, bool b_kn, bool exact, int bits, bool use_corr, int[] streams, int[] events, bool used) "
+      "-> ()");
+  ops.def(
       "fp64_emu_gemm_checked(Tensor! out, Tensor! ws, Tensor A, Tensor B, Tensor primes_cpu, bool b_kn, bool "
       "exact, int bits, bool use_corr) -> ()");
   ops.def("fp64_emu_status(Tensor ws) -> int");
@@ -353,6 +409,7 @@ TORCH_LIBRARY_IMPL(fp64_emu_b200, CUDA, ops) {
   ops.impl("fp64_emu_gemm_ws", &gemm_ws);
   ops.impl("fp64_emu_gemm_ws_ev", &gemm_ws_ev);
   ops.impl("fp64_emu_gemm_checked", &gemm_checked);
+  ops.impl("fp64_emu_host_submit", &host_submit);   // CPU operands, CUDA buffers: the CUDA key
   ops.impl("fp64_emu_status", &status);
   ops.impl("fp64_emu_debug_fetch", &debug_fetch);
 }

@@ -35,8 +35,15 @@ class HostStream:
         self.h2d = torch.cuda.Stream(self.device)
         self.comp = torch.cuda.Stream(self.device)
         self.d2h = torch.cuda.Stream(self.device)
+        self._streams = [self.h2d.cuda_stream, self.comp.cuda_stream, self.d2h.cuda_stream]
+        self._caller = self._event()
         self.slots = [None] * self.depth
         self.n = 0
+
+    def _event(self):
+        ev = torch.cuda.Event()
+        ev.record(torch.cuda.current_stream(self.device))   # creates the CUDA event
+        return ev
 
     def _slot(self, i, A, B):
         """Device buffers of slot i for operands shaped like A and B."""
@@ -59,8 +66,7 @@ class HostStream:
                 ws = torch.empty(ops.fp64_emu_workspace_bytes(Ad, Bd, primes, self.b_kn, corr), dtype=torch.uint8,
                                  device=dev)
             s = {"A": Ad, "B": Bd, "C": Cd, "ws": ws, "primes": primes, "corr": corr,
-                 "loaded": torch.cuda.Event(), "computed": torch.cuda.Event(), "done": torch.cuda.Event(),
-                 "used": False}
+                 "loaded": self._event(), "computed": self._event(), "done": self._event(), "used": False}
             self.slots[i] = s
         return s
 
@@ -70,26 +76,16 @@ class HostStream:
         and `out` unread until synchronize()."""
         if A.is_cuda or B.is_cuda or out.is_cuda:
             raise RuntimeError("HostStream.submit takes CPU tensors")
+        if A.dtype != torch.float64 or B.dtype != torch.float64 or out.dtype != torch.float64:
+            raise RuntimeError("HostStream.submit takes float64 tensors")
+        A, B = A.contiguous(), B.contiguous()
         s = self._slot(self.n % self.depth, A, B)
-        cur = torch.cuda.current_stream(self.device)
-        for st in (self.h2d, self.comp, self.d2h):
-            st.wait_stream(cur)                       # work the caller queued before this call
-        if s["used"]:
-            self.h2d.wait_event(s["computed"])        # the slot's previous product has read its operands
-            self.comp.wait_event(s["done"])           # ... and its result has left the device
-        with torch.cuda.stream(self.h2d):
-            s["A"].copy_(A, non_blocking=True)
-            s["B"].copy_(B, non_blocking=True)
-            s["loaded"].record(self.h2d)
-        self.comp.wait_event(s["loaded"])
-        with torch.cuda.stream(self.comp):
-            ops.fp64_emu_gemm_ws(s["C"], s["ws"], s["A"], s["B"], s["primes"], self.b_kn, self.exact, self.bits,
-                                 s["corr"], 15, 0)
-            s["computed"].record(self.comp)
-        self.d2h.wait_event(s["computed"])
-        with torch.cuda.stream(self.d2h):
-            out.copy_(s["C"], non_blocking=True)
-            s["done"].record(self.d2h)
+        # one native call queues the operand copies, the product and the
+        # result copy on the three streams, ordered by the slot's events
+        ops.fp64_emu_host_submit(out, A, B, s["A"], s["B"], s["C"], s["ws"], s["primes"], self.b_kn, self.exact,
+                                 self.bits, s["corr"], self._streams,
+                                 [self._caller.cuda_event, s["loaded"].cuda_event, s["computed"].cuda_event,
+                                  s["done"].cuda_event], s["used"])
         s["used"] = True
         self.n += 1
         return out

@@ -123,3 +123,30 @@ def test_host_stream_batched(emu):
     hs.submit(A, B, out)
     hs.synchronize()
     assert torch.equal(out, emu.bmm(A.cuda(), B.cuda()).cpu())
+
+
+def test_host_stream_depth_one_many_small(emu):
+    # one slot reused by every product: each one's copies wait for the previous
+    # product to read its operands and for its result to leave the device
+    g = torch.Generator(device="cuda").manual_seed(9)
+    hs = emu.HostStream("mm_nt", depth=1)
+    jobs, outs = [], []
+    for i in range(12):
+        A = torch.randn(96, 300, dtype=torch.float64, device="cuda", generator=g)
+        Bt = torch.randn(300, 80, dtype=torch.float64, device="cuda", generator=g)
+        out = torch.empty(96, 80, dtype=torch.float64).pin_memory()
+        hs.submit(A.cpu().pin_memory(), Bt.cpu().pin_memory(), out)
+        jobs.append((A, Bt))
+        outs.append(out)
+    hs.synchronize()
+    for (A, Bt), out in zip(jobs, outs):
+        assert torch.equal(out, emu.mm_nt(A, Bt).cpu())
+
+
+def test_host_stream_rejects_strided_out(emu):
+    hs = emu.HostStream("mm_nt")
+    A = torch.randn(16, 32, dtype=torch.float64)
+    Bt = torch.randn(32, 8, dtype=torch.float64)
+    out = torch.empty(8, 16, dtype=torch.float64).t()
+    with pytest.raises(RuntimeError):
+        hs.submit(A, Bt, out)

@@ -10,9 +10,11 @@ the two sizing maxima; total work is fixed, so scaling is "strong".
 
   value   device time (CUDA events, max over ranks) per step with inputs
           resident in HBM, as emulated FP64 TFLOP/s = 2MNK / t
-  e2e     the same through the public API (fp64_emu.mm_nt, or the
-          partitioned path) with each step's inputs copied from pinned host
-          memory and the product copied back inside the timed region
+  e2e     the same through the public API with each step's inputs copied
+          from pinned host memory and the product copied back inside the
+          timed region: fp64_emu.HostStream at N = 1 (copies and products of
+          neighbouring steps overlapped), fp64_emu.dist.ShardedHostStream at
+          N > 1
   roofline  the modular tensor-core GEMM (the dominant kernel): INT8 ops
           per launch / its average duration over the timed region
   accuracy  the metric's "correct bits vs dd": after timing, the product's

@@ -46,6 +46,7 @@ constexpr int64_t kNtMaxK = 131071;              // single-launch int32 bound (f
 constexpr int64_t kSegK = 65536;                 // deep-K segment depth
 constexpr int64_t kMaxK = 128 * kSegK;           // 8,388,608
 constexpr int64_t kFusedCorrMaxK = 65536;        // 2 K 127^2 < 2^31
+constexpr int64_t kB200Sms = 148;                 // CTAs of one wave of the GEMM kernels
 
 int fail(int code, const char* fmt, ...) {
   char buf[512];
@@ -251,8 +252,22 @@ int make_plan(const f64e_problem* p, Plan* L) {
   l.nseg = l.deep ? (int)((p->K + kSegK - 1) / kSegK) : 1;
   l.Kp = round_up(std::max<int64_t>(l.Kseg, 1), 16);
   l.ldn = round_up(std::max<int64_t>(l.N, 1), 16);
-  if (!l.use_corr) l.gemm_corr = 0;
-  else l.gemm_corr = (l.Kseg <= kFusedCorrMaxK) ? 1 : 2;
+  if (!l.use_corr) {
+    l.gemm_corr = 0;
+  } else if (l.Kseg > kFusedCorrMaxK) {
+    l.gemm_corr = 2;
+  } else {
+    // The fused correction slot runs a K loop twice as long as a residue
+    // slot.  When the whole GEMM is one wave of tiles (one per CTA, or per
+    // CTA pair) that slot alone sets the kernel's time, so such products
+    // keep the two correction products as separate planes: the same integers,
+    // summed by the reconstruction.  (The deep-K accumulation takes one
+    // fused plane per segment.)
+    const bool pair = gemm_use_pair((int)std::min<int64_t>(l.M, INT32_MAX));
+    const int64_t bm = pair ? 2 * gemm_pair_block_rows() : gemm_block_rows_a();
+    const int64_t fused_tiles = ((l.M + bm - 1) / bm) * ((l.N + 255) / 256) * (l.P + 1) * l.batch;
+    l.gemm_corr = (!l.deep && fused_tiles <= (pair ? kB200Sms / 2 : kB200Sms)) ? 2 : 1;
+  }
   if (!l.use_corr) l.recon_corr = 0;
   else l.recon_corr = l.deep ? 3 : l.gemm_corr;
   l.kslab = 0;

@@ -240,16 +240,19 @@ def max_over_ranks(x):
     return float(t.item())
 
 
-def our_kernel_launches_per_step(kind, batch, chunks):
-    # sizing: row stats of A + column partials + column finalize with the
-    # operand maxima (B as [K, N]), or one launch for both operands' row stats
-    # and the maxima; per chunk one extraction of A, one GEMM and one
-    # reconstruction; B extracted once (single product) or per chunk (batch).
-    # (Products small enough to extract both operands in one launch do not
-    # occur in the bench's workloads.)
+def our_kernel_launches_per_step(kind, batch, chunks, M=None, N=None, K=None):
+    # sizing: A's row statistics with B's column partials in one launch, then
+    # the column finalize with the operand maxima (B as [K, N]), or one launch
+    # for both operands' row statistics and the maxima; per chunk one
+    # extraction of A, one GEMM and one reconstruction; B extracted once
+    # (single product) or per chunk (batch).  An unchunked product of at most
+    # 4 M operand elements extracts both operands in one launch.
     nt = kind in ("mm_nt", "bmm_nt")
     c = max(1, chunks)
-    return (3 if nt else 1) + 3 * c + (1 if batch == 1 else c)
+    n = (2 if nt else 1) + 3 * c + (1 if batch == 1 else c)
+    if c == 1 and None not in (M, N, K) and (batch * M + batch * N) * K <= (1 << 22):
+        n -= 1
+    return n
 
 
 def cpu_baseline_oracle(A_cpu, Bt_cpu, nprimes, corr, rows):
@@ -458,7 +461,7 @@ def run_ours(args):
                         "overlap)") if world == 1 else
                        ("fp64_emu.dist.ShardedHostStream (disjoint host shares, NVLink all-gathers, overlapped "
                         "stages)" if shs is not None else "fp64_emu.dist.ShardedProduct with explicit copies")},
-        "gpu_launches": sum(our_kernel_launches_per_step(kind, A_l.shape[0] if A_l.dim() == 3 else 1, c)
+        "gpu_launches": sum(our_kernel_launches_per_step(kind, A_l.shape[0] if A_l.dim() == 3 else 1, c, Ml, Nl, Kl)
                             for c in launches),
         "roofline": {"bound": "tensor", "kernel": "residue_gemm_pair_kernel" if Ml > 128 else "residue_gemm_tc_kernel",
                      "achieved": round(achieved, 1), "peak": round(peak, 1), "unit": "TOPS (int8)",

@@ -337,10 +337,9 @@ int run_sizing(const Plan& l, const double* A, const double* B, void* ws, cudaSt
   cudaError_t e = cudaMemsetAsync(&head->status, 0, 2 * sizeof(int32_t), s);
   if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync");
   if (l.nt) {
-    launch_row_stats(A, l.MF, l.K, l.bits, at<int16_t>(ws, l.o_sftA), at<float>(ws, l.o_lgA), s);
-    launch_col_stats_maxlg(B, l.batch, l.K, l.N, l.kslab, l.nslab, l.bits, at<int16_t>(ws, l.o_sftB),
-                           at<float>(ws, l.o_lgB), at<double>(ws, l.o_pmax), at<double>(ws, l.o_pss),
-                           at<float>(ws, l.o_lgA), l.MF, head->maxlg, &head->counter, s);
+    launch_nt_stats_maxlg(A, l.MF, B, l.batch, l.K, l.N, l.kslab, l.nslab, l.bits, at<int16_t>(ws, l.o_sftA),
+                          at<float>(ws, l.o_lgA), at<int16_t>(ws, l.o_sftB), at<float>(ws, l.o_lgB),
+                          at<double>(ws, l.o_pmax), at<double>(ws, l.o_pss), head->maxlg, &head->counter, s);
   } else {
     launch_rows_stats_both(A, l.MF, B, l.NF, l.K, l.bits, at<int16_t>(ws, l.o_sftA), at<float>(ws, l.o_lgA),
                            at<int16_t>(ws, l.o_sftB), at<float>(ws, l.o_lgB), head->maxlg, &head->counter, s);
@@ -494,12 +493,13 @@ void extract_B(const Plan& l, const ModTables& T, const View& v, void* ws, int64
   else launch_extract_rows(eb, T, s);
 }
 
-// Both operands of a view; one launch for two [rows, K] operands of a small
-// product (where launch latency, not the extraction, dominates).
+// Both operands of a view; one launch for both operands of a small product
+// (where launch latency, not the extraction, dominates).
 void extract_AB(const Plan& l, const ModTables& T, const View& v, void* ws, int64_t k0, int64_t kw, cudaStream_t s) {
   constexpr int64_t kPairMaxElems = int64_t(1) << 22;
-  if (!l.nt && (v.batch * v.M + v.batch * v.N) * kw <= kPairMaxElems) {
-    launch_extract_rows_pair(extract_A_args(l, v, ws, k0, kw), extract_B_args(l, v, ws, k0, kw), T, s);
+  if ((v.batch * v.M + v.batch * v.N) * kw <= kPairMaxElems) {
+    if (l.nt) launch_extract_nt_pair(extract_A_args(l, v, ws, k0, kw), extract_B_args(l, v, ws, k0, kw), T, s);
+    else launch_extract_rows_pair(extract_A_args(l, v, ws, k0, kw), extract_B_args(l, v, ws, k0, kw), T, s);
     return;
   }
   extract_A(l, T, v, ws, k0, kw, s);

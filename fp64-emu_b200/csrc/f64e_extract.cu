@@ -235,27 +235,23 @@ __device__ __forceinline__ void extract8(const double (&x)[8], int s, bool fast,
   if (!CORR_FIRST) store_corr(S, corr, a, dst);
 }
 
-// [rows, K] operand: thread (x, y) of a (32, 8) block handles 8 consecutive
-// columns of one row; a warp covers 256 columns (2 KB read, 256 B written per
-// plane, both contiguous).
-// PAIR: two operands in one launch, blockIdx.z selecting the arguments
-// (small products, where launches dominate).  Three blocks per SM (79
-// registers, no spills): the kernel waits on its loads, and the third block
-// hides more of that than the register cap costs (measured: 8192^2 operands
-// extract in 0.92-0.95 ms against 1.03-1.07 ms at two blocks).
-template <bool VEC, bool PAIR>
-__global__ void __launch_bounds__(256, 3) extract_rows_kernel(const ExtractPair ap, const ModTables T) {
-  const ExtractArgs& a = ap.a[PAIR ? blockIdx.z : 0];
+// [rows, K] operand: thread (tx, ty) of a 256-thread block (32 x 8) handles
+// 8 consecutive columns of one row; a warp covers 256 columns (2 KB read,
+// 256 B written per plane, both contiguous).  (bx, by) of a (gdx, gdy) grid,
+// with grid-stride loops over the K chunks and the rows.
+template <bool VEC>
+__device__ __forceinline__ void extract_rows_body(const ExtractArgs& a, const ModTables& T, int bx, int by, int gdx,
+                                                  int gdy, int tx, int ty) {
   const Gain gn = pick_gain(a.maxlg[0], a.maxlg[1], T.log2M, a.bits);
   const int be = gn.bits_eff;
   const bool corr = a.use_corr != 0;
   const int64_t nch = a.Kp >> 3;
-  for (int64_t r = (int64_t)blockIdx.y * 8 + threadIdx.y; r < a.rows; r += (int64_t)gridDim.y * 8) {
+  for (int64_t r = (int64_t)by * 8 + ty; r < a.rows; r += (int64_t)gdy * 8) {
     const int s = (int)a.sft[r] + gn.g;
     const bool row_fast = (s >= -960) && (s <= 960);
     const double p2s = pow2d(row_fast ? s : 0), p2h = pow2d(7 - be);
     const double* __restrict__ xr = a.X + r * a.ld + a.koff;
-    for (int64_t ch = (int64_t)blockIdx.x * 32 + threadIdx.x; ch < nch; ch += (int64_t)gridDim.x * 32) {
+    for (int64_t ch = (int64_t)bx * 32 + tx; ch < nch; ch += (int64_t)gdx * 32) {
       const int64_t k0 = ch << 3;
       double x[8];
       if (VEC && k0 + 8 <= a.K) {
@@ -275,6 +271,17 @@ __global__ void __launch_bounds__(256, 3) extract_rows_kernel(const ExtractPair 
   }
 }
 
+// PAIR: two [rows, K] operands in one launch, blockIdx.z selecting the
+// arguments (small products, where launches dominate).  Three blocks per SM
+// (79 registers, no spills): the kernel waits on its loads, and the third
+// block hides more of that than the register cap costs (measured: 8192^2
+// operands extract in 0.92-0.95 ms against 1.03-1.07 ms at two blocks).
+template <bool VEC, bool PAIR>
+__global__ void __launch_bounds__(256, 3) extract_rows_kernel(const ExtractPair ap, const ModTables T) {
+  extract_rows_body<VEC>(ap.a[PAIR ? blockIdx.z : 0], T, (int)blockIdx.x, (int)blockIdx.y, (int)gridDim.x,
+                         (int)gridDim.y, (int)threadIdx.x, (int)threadIdx.y);
+}
+
 // [batch, K, N] operand: a block takes a 64 (k) x 32 (n) tile.  Warp w reads
 // the rows k0 + w + 8 i (32 consecutive n, 256 B each) and parks the doubles
 // transposed in shared memory, 66 per n (16.5 KB); thread (n, kg) then splits
@@ -285,10 +292,13 @@ __global__ void __launch_bounds__(256, 3) extract_rows_kernel(const ExtractPair 
 // chunks puts them in 8 different bank groups.
 constexpr int kColTileK = 64, kColTileN = 32, kColPitch = 66;
 
-__global__ void __launch_bounds__(256, 2) extract_cols_kernel(const ExtractArgs a, const ModTables T) {
-  __shared__ __align__(16) double xs[kColTileN * kColPitch];
-  const int64_t b = blockIdx.z;
-  const int64_t n0 = (int64_t)blockIdx.x * kColTileN, k0 = (int64_t)blockIdx.y * kColTileK;
+// Tile (bx: n tiles, by: K tiles, bz: batch member) of a [batch, K, N]
+// operand, by a 256-thread block with xs[kColTileN * kColPitch] of shared
+// memory.  One barrier, reached by every thread of the block.
+__device__ __forceinline__ void extract_cols_body(const ExtractArgs& a, const ModTables& T, int bx, int by, int bz,
+                                                  double* xs) {
+  const int64_t b = bz;
+  const int64_t n0 = (int64_t)bx * kColTileN, k0 = (int64_t)by * kColTileK;
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
   {
     const int64_t n = n0 + lane;
@@ -320,7 +330,30 @@ __global__ void __launch_bounds__(256, 2) extract_cols_kernel(const ExtractArgs 
   const int s = (int)a.sft[b * a.N + n] + gn.g;
   const bool fast = (s >= -960) && (s <= 960);
   extract8<true>(x, s, fast, pow2d(fast ? s : 0), pow2d(7 - be), be, a.use_corr != 0, a, T,
-           a.planes + (b * a.N + n) * a.Kp + kk);
+                 a.planes + (b * a.N + n) * a.Kp + kk);
+}
+
+__global__ void __launch_bounds__(256, 2) extract_cols_kernel(const ExtractArgs a, const ModTables T) {
+  __shared__ __align__(16) double xs[kColTileN * kColPitch];
+  extract_cols_body(a, T, (int)blockIdx.x, (int)blockIdx.y, (int)blockIdx.z, xs);
+}
+
+// A [rows, K] operand and a [batch, K, N] operand in one launch (small nt
+// products, where launches dominate): blocks [0, na) take the first as a
+// (gxa, na / gxa) grid, the rest the second's (gxb, gyb, batch) tiles.
+template <bool VEC>
+__global__ void __launch_bounds__(256, 2) extract_nt_pair_kernel(const ExtractArgs ra, const ExtractArgs cb,
+                                                                 const ModTables T, int gxa, int na, int gxb,
+                                                                 int gyb) {
+  __shared__ __align__(16) double xs[kColTileN * kColPitch];
+  const int i = (int)blockIdx.x;
+  if (i < na) {
+    extract_rows_body<VEC>(ra, T, i % gxa, i / gxa, gxa, na / gxa, (int)(threadIdx.x & 31), (int)(threadIdx.x >> 5));
+  } else {
+    const int j = i - na, per = gxb * gyb;
+    const int bz = j / per, r = j - bz * per;
+    extract_cols_body(cb, T, r % gxb, r / gxb, bz, xs);
+  }
 }
 
 namespace {
@@ -355,6 +388,29 @@ void launch_extract_rows_pair(const ExtractArgs& a0, const ExtractArgs& a1, cons
   ap.a[1] = a1;
   if (rows_vec(a0) && rows_vec(a1)) extract_rows_kernel<true, true><<<dim3(gx, gy, 2), dim3(32, 8), 0, s>>>(ap, T);
   else extract_rows_kernel<false, true><<<dim3(gx, gy, 2), dim3(32, 8), 0, s>>>(ap, T);
+}
+
+void launch_extract_nt_pair(const ExtractArgs& ra, const ExtractArgs& cb, const ModTables& T, cudaStream_t s) {
+  if (ra.rows <= 0 || ra.Kp <= 0 || cb.N <= 0 || cb.batch <= 0) {
+    launch_extract_rows(ra, T, s);
+    launch_extract_cols(cb, T, s);
+    return;
+  }
+  const int64_t nch = ra.Kp >> 3;
+  const int64_t gxa = std::min<int64_t>((nch + 31) / 32, 1 << 20);
+  const int64_t gya = std::min<int64_t>((ra.rows + 7) / 8, 65535);
+  const int64_t gxb = (cb.N + kColTileN - 1) / kColTileN, gyb = (cb.Kp + kColTileK - 1) / kColTileK;
+  const int64_t na = gxa * gya, nb = gxb * gyb * cb.batch;
+  if (na + nb > INT32_MAX) {
+    launch_extract_rows(ra, T, s);
+    launch_extract_cols(cb, T, s);
+    return;
+  }
+  const unsigned grid = (unsigned)(na + nb);
+  if (rows_vec(ra))
+    extract_nt_pair_kernel<true><<<grid, 256, 0, s>>>(ra, cb, T, (int)gxa, (int)na, (int)gxb, (int)gyb);
+  else
+    extract_nt_pair_kernel<false><<<grid, 256, 0, s>>>(ra, cb, T, (int)gxa, (int)na, (int)gxb, (int)gyb);
 }
 
 void launch_extract_cols(const ExtractArgs& a, const ModTables& T, cudaStream_t s) {

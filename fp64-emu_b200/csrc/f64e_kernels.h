@@ -13,19 +13,18 @@
 namespace f64e {
 
 // ---- sizing (f64e_sizing.cu) ----
-void launch_row_stats(const double* X, int64_t rows, int64_t cols, int bits, int16_t* sft, float* lg,
-                      cudaStream_t s);
 void col_slabs(int64_t NF, int64_t K, int64_t* kslab, int* nslab);
 // Both operands as [rows, K] in one launch, operand maxima included (counter
 // zeroed before the launch).
 void launch_rows_stats_both(const double* A, int64_t ra, const double* B, int64_t rb, int64_t cols, int bits,
                             int16_t* sftA, float* lgA, int16_t* sftB, float* lgB, float* maxlg, unsigned* counter,
                             cudaStream_t s);
-// Column statistics of a [batch, K, N] operand plus the operand maxima (A's
-// row statistics already in lgA; counter zeroed before the launch).
-void launch_col_stats_maxlg(const double* X, int64_t batch, int64_t K, int64_t N, int64_t kslab, int nslab,
-                            int bits, int16_t* sft, float* lg, double* pmax, double* pss, const float* lgA,
-                            int64_t ra, float* maxlg, unsigned* counter, cudaStream_t s);
+// A's row statistics, B's column statistics ([batch, K, N]) and the operand
+// maxima: one launch for the row statistics and column partials, one for the
+// column finalize (whose last CTA takes the maxima; counter zeroed before).
+void launch_nt_stats_maxlg(const double* A, int64_t ra, const double* X, int64_t batch, int64_t K, int64_t N,
+                           int64_t kslab, int nslab, int bits, int16_t* sftA, float* lgA, int16_t* sft, float* lg,
+                           double* pmax, double* pss, float* maxlg, unsigned* counter, cudaStream_t s);
 
 // ---- extraction (f64e_extract.cu) ----
 // Planes are K-major int8: plane t lives at planes + t * pstride (rows * Kp
@@ -55,6 +54,8 @@ void launch_extract_rows(const ExtractArgs& a, const ModTables& T, cudaStream_t 
 // Two [rows, K] operands with the same Kp in one launch.
 void launch_extract_rows_pair(const ExtractArgs& a0, const ExtractArgs& a1, const ModTables& T, cudaStream_t s);
 void launch_extract_cols(const ExtractArgs& a, const ModTables& T, cudaStream_t s);  // X is [batch, K, N]
+// A [rows, K] operand (ra) and a [batch, K, N] operand (cb) in one launch.
+void launch_extract_nt_pair(const ExtractArgs& ra, const ExtractArgs& cb, const ModTables& T, cudaStream_t s);
 
 // ---- modular GEMM (f64e_gemm.cu) ----
 struct GemmArgs {

@@ -139,15 +139,16 @@ __global__ void __launch_bounds__(256) rows_stats_both_kernel(const double* __re
   if (last_block_done(counter)) maxlg_block(lgA, ra, lgB, rb, maxlg);
 }
 
-// Column partials over one K slab per blockIdx.y: thread j owns global column
-// j of a [batch, K, N] operand (member j / N), reads coalesced across columns.
-__global__ void __launch_bounds__(256) col_partial_kernel(const double* __restrict__ X, int64_t totalcols,
-                                                          int64_t K, int64_t N, int64_t kslab,
-                                                          double* __restrict__ pmax, double* __restrict__ pss) {
-  const int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+// Column partials over K slab `slab`: thread j of column block bx owns global
+// column j of a [batch, K, N] operand (member j / N), reads coalesced across
+// columns.  No barrier.
+__device__ __forceinline__ void col_partial_one(const double* __restrict__ X, int64_t totalcols, int64_t K,
+                                                int64_t N, int64_t kslab, int64_t bx, int64_t slab,
+                                                double* __restrict__ pmax, double* __restrict__ pss) {
+  const int64_t j = bx * 256 + threadIdx.x;
   if (j >= totalcols) return;
   const int64_t b = j / N, n = j - b * N;
-  const int64_t k0 = (int64_t)blockIdx.y * kslab;
+  const int64_t k0 = slab * kslab;
   const int64_t k1 = min(k0 + kslab, K);
   const double* __restrict__ base = X + b * K * N + n;
   double mx = 0.0, ss = 0.0;
@@ -168,8 +169,31 @@ __global__ void __launch_bounds__(256) col_partial_kernel(const double* __restri
     mx = fmax(mx, fabs(v));
     ss = fma(v, v, ss);
   }
-  pmax[(int64_t)blockIdx.y * totalcols + j] = mx;
-  pss[(int64_t)blockIdx.y * totalcols + j] = ss;
+  pmax[slab * totalcols + j] = mx;
+  pss[slab * totalcols + j] = ss;
+}
+
+__global__ void __launch_bounds__(256) col_partial_kernel(const double* __restrict__ X, int64_t totalcols,
+                                                          int64_t K, int64_t N, int64_t kslab,
+                                                          double* __restrict__ pmax, double* __restrict__ pss) {
+  col_partial_one(X, totalcols, K, N, kslab, blockIdx.x, blockIdx.y, pmax, pss);
+}
+
+// A's row statistics and B's column partials in one launch (the operands of
+// an nt product): CTAs [0, ncb) take the (column block, K slab) pairs of B,
+// gx column blocks per slab (each thread a long sequential chain, so they
+// start first), the rest A's rows (stride nrb).
+__global__ void __launch_bounds__(256) nt_stats_kernel(const double* __restrict__ A, int64_t rows, int64_t cols,
+                                                       int bits, int16_t* __restrict__ sftA, float* __restrict__ lgA,
+                                                       int64_t nrb, const double* __restrict__ B, int64_t totalcols,
+                                                       int64_t K, int64_t N, int64_t kslab, int64_t gx, int64_t ncb,
+                                                       double* __restrict__ pmax, double* __restrict__ pss) {
+  const int64_t i = blockIdx.x;
+  if (i < ncb) {
+    col_partial_one(B, totalcols, K, N, kslab, i % gx, i / gx, pmax, pss);
+  } else {
+    for (int64_t r = i - ncb; r < rows; r += nrb) row_stats_one(A + r * cols, cols, bits, &sftA[r], &lgA[r]);
+  }
 }
 
 // Column finalize of B plus the operand maxima by the last CTA to finish.
@@ -207,13 +231,6 @@ __global__ void __launch_bounds__(256) col_finalize_maxlg_kernel(const double* _
   if (last_block_done(counter)) maxlg_block(lgA, ra, lg, totalcols, maxlg);
 }
 
-void launch_row_stats(const double* X, int64_t rows, int64_t cols, int bits, int16_t* sft, float* lg,
-                      cudaStream_t s) {
-  if (rows <= 0) return;
-  const unsigned grid = (unsigned)std::min<int64_t>(rows, 1 << 30);
-  row_stats_kernel<<<grid, 256, 0, s>>>(X, rows, cols, bits, sft, lg);
-}
-
 void col_slabs(int64_t NF, int64_t K, int64_t* kslab, int* nslab) {
   int64_t nsl0 = 131072 / std::max<int64_t>(NF, 1);
   nsl0 = std::min<int64_t>(std::max<int64_t>(nsl0, 1), 128);
@@ -228,12 +245,22 @@ void launch_rows_stats_both(const double* A, int64_t ra, const double* B, int64_
   rows_stats_both_kernel<<<grid, 256, 0, s>>>(A, ra, B, rb, cols, bits, sftA, lgA, sftB, lgB, maxlg, counter);
 }
 
-void launch_col_stats_maxlg(const double* X, int64_t batch, int64_t K, int64_t N, int64_t kslab, int nslab,
-                            int bits, int16_t* sft, float* lg, double* pmax, double* pss, const float* lgA,
-                            int64_t ra, float* maxlg, unsigned* counter, cudaStream_t s) {
+void launch_nt_stats_maxlg(const double* A, int64_t ra, const double* X, int64_t batch, int64_t K, int64_t N,
+                           int64_t kslab, int nslab, int bits, int16_t* sftA, float* lgA, int16_t* sft, float* lg,
+                           double* pmax, double* pss, float* maxlg, unsigned* counter, cudaStream_t s) {
   const int64_t NF = batch * N;
-  const unsigned gx = (unsigned)std::max<int64_t>(1, (NF + 255) / 256);
-  if (nslab > 0 && NF > 0) col_partial_kernel<<<dim3(gx, nslab), 256, 0, s>>>(X, NF, K, N, kslab, pmax, pss);
+  const int64_t gx = std::max<int64_t>(1, (NF + 255) / 256);
+  const int64_t nrb = std::min<int64_t>(ra, 1 << 30);
+  const int64_t ncb = (nslab > 0 && NF > 0) ? gx * nslab : 0;
+  if (nrb + ncb > 0) {
+    if (nrb + ncb <= INT32_MAX) {
+      nt_stats_kernel<<<(unsigned)(nrb + ncb), 256, 0, s>>>(A, ra, K, bits, sftA, lgA, nrb, X, NF, K, N, kslab, gx,
+                                                            ncb, pmax, pss);
+    } else {
+      if (ra > 0) row_stats_kernel<<<(unsigned)nrb, 256, 0, s>>>(A, ra, K, bits, sftA, lgA);
+      if (ncb > 0) col_partial_kernel<<<dim3((unsigned)gx, nslab), 256, 0, s>>>(X, NF, K, N, kslab, pmax, pss);
+    }
+  }
   const unsigned gf = (unsigned)std::max<int64_t>(1, (NF + 7) / 8);   // a warp per column
   col_finalize_maxlg_kernel<<<gf, 256, 0, s>>>(pmax, pss, NF, nslab, bits, sft, lg, lgA, ra, maxlg, counter);
 }

@@ -42,9 +42,11 @@ def test_peaks_and_traffic_from_committed_files():
 
 
 def test_launch_count_claim():
-    # mm_nt: three sizing launches; per chunk extraction of A, GEMM and
+    # mm_nt: two sizing launches; per chunk extraction of A, GEMM and
     # reconstruction; B extracted once for a single product
-    assert bench.our_kernel_launches_per_step("mm_nt", 1, 5) == 3 + 15 + 1
+    assert bench.our_kernel_launches_per_step("mm_nt", 1, 5, 8192, 8192, 8192) == 2 + 15 + 1
     # mm: one sizing launch; a batch extracts B with every member chunk
-    assert bench.our_kernel_launches_per_step("mm", 1, 1) == 1 + 3 + 1
-    assert bench.our_kernel_launches_per_step("bmm_nt", 64, 8) == 3 + 24 + 8
+    assert bench.our_kernel_launches_per_step("mm", 1, 1, 4096, 4096, 4096) == 1 + 3 + 1
+    assert bench.our_kernel_launches_per_step("bmm_nt", 64, 8, 1024, 1024, 1024) == 2 + 24 + 8
+    # a small unchunked product extracts both operands in one launch (C1)
+    assert bench.our_kernel_launches_per_step("mm_nt", 1, 1, 128, 128, 4096) == 2 + 1 + 1 + 1

@@ -1071,6 +1071,20 @@ int f64e_status(const void* ws, void* stream, int32_t* status) {
 
 void f64e_set_wait_limit_ns(uint64_t ns) { g_wait_limit.store(ns ? ns : 1); }
 
+int f64e_wait_selftest(void* ws, size_t ws_bytes, uint64_t limit_ns, void* stream, int32_t* status) {
+  g_err.clear();
+  if (!ws || !status || ws_bytes < sizeof(WsHead)) return fail(F64E_ERR_ARGUMENT, "workspace of a WsHead at least");
+  if (limit_ns == 0 || limit_ns > 10000000000ULL) return fail(F64E_ERR_ARGUMENT, "limit must be in (0, 10 s]");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  WsHead* head = static_cast<WsHead*>(ws);
+  cudaError_t e = cudaMemsetAsync(&head->status, 0, sizeof(int32_t), s);
+  if (e == cudaSuccess) e = launch_wait_selftest(&head->status, limit_ns, s);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(status, &head->status, sizeof(int32_t), cudaMemcpyDeviceToHost, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  if (e != cudaSuccess) return cuda_fail(e, "wait self-test");
+  return F64E_OK;
+}
+
 const char* f64e_last_error(void) { return g_err.c_str(); }
 
 int f64e_debug_fetch(const f64e_problem* p, const void* ws, int which, void* host, size_t cap, size_t* nbytes,

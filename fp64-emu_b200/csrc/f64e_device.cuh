@@ -21,6 +21,7 @@ enum : int {
   kWaitAccFull = 3,   // epilogue waiting for an accumulator
   kWaitAccEmpty = 4,  // MMA issuer waiting for the epilogue to drain TMEM
   kWaitDrain = 5,     // teardown waiting for in-flight copies / MMAs
+  kWaitSelfTest = 9,  // f64e_wait_selftest: a barrier nothing arrives at
 };
 
 __device__ __forceinline__ uint64_t globaltimer_ns() {

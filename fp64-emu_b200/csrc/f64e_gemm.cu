@@ -502,6 +502,21 @@ int gemm_block_rows_b() { return BN; }
 int gemm_pair_block_rows() { return PHALF; }
 bool gemm_use_pair(int M) { return M > BM; }
 
+// One thread waits, with the GEMM's bounded wait, on an mbarrier that nothing
+// arrives at: the wait runs out after limit_ns and records kWaitSelfTest in
+// the status word.  Nothing else is in flight, so the kernel simply returns.
+__global__ void wait_selftest_kernel(int* status, uint64_t limit_ns) {
+  __shared__ __align__(8) uint64_t bar;
+  mbar_init(&bar, 1);
+  fence_barrier_init();
+  mbar_wait(&bar, 0, limit_ns, status, kWaitSelfTest);
+}
+
+cudaError_t launch_wait_selftest(int* status, uint64_t limit_ns, cudaStream_t s) {
+  wait_selftest_kernel<<<1, 1, 0, s>>>(status, limit_ns);
+  return cudaGetLastError();
+}
+
 cudaError_t launch_residue_gemm(const CUtensorMap& tA, const CUtensorMap& tB, const GemmArgs& g, const ModTables& T,
                                 int num_sms, cudaStream_t s) {
   const int ntm = (g.M + BM - 1) / BM, ntn = (g.N + BN - 1) / BN;

@@ -77,6 +77,8 @@ int gemm_block_rows_a();
 int gemm_block_rows_b();
 int gemm_pair_block_rows();   // box rows of both operands in the CTA-pair kernel
 bool gemm_use_pair(int M);    // CTA-pair kernel for tall problems
+// A bounded wait that runs out on purpose (one thread, no copies in flight).
+cudaError_t launch_wait_selftest(int* status, uint64_t limit_ns, cudaStream_t s);
 cudaError_t launch_residue_gemm(const CUtensorMap& tA, const CUtensorMap& tB, const GemmArgs& g, const ModTables& T,
                                 int num_sms, cudaStream_t s);
 cudaError_t launch_residue_gemm_pair(const CUtensorMap& tA, const CUtensorMap& tB, const GemmArgs& g,

@@ -349,6 +349,16 @@ at::Tensor debug_fetch(const at::Tensor& ws, const at::Tensor& A, const at::Tens
 
 void set_wait_limit_ns(int64_t ns) { f64e_set_wait_limit_ns((uint64_t)ns); }
 
+int64_t wait_selftest(at::Tensor& ws, int64_t limit_ns) {
+  TORCH_CHECK(ws.is_cuda() && ws.is_contiguous(), "workspace must be a contiguous CUDA tensor");
+  TORCH_CHECK(limit_ns > 0, "limit must be positive");
+  const c10::cuda::CUDAGuard guard(ws.device());
+  int32_t st = 0;
+  check(f64e_wait_selftest(ws.data_ptr(), (size_t)ws.numel() * ws.element_size(), (uint64_t)limit_ns, stream_of(),
+                           &st));
+  return st;
+}
+
 }  // namespace
 
 TORCH_LIBRARY(fp64_emu_b200, ops) {
@@ -392,6 +402,7 @@ TORCH_LIBRARY(fp64_emu_b200, ops) {
       "fp64_emu_debug_fetch(Tensor ws, Tensor A, Tensor B, Tensor primes_cpu, bool b_kn, bool use_corr, int which) "
       "-> Tensor");
   ops.def("fp64_emu_set_wait_limit_ns(int ns) -> ()");
+  ops.def("fp64_emu_wait_selftest(Tensor! ws, int limit_ns) -> int");
   ops.impl("fp64_emu_maxp", &maxp);
   ops.impl("fp64_emu_workspace_bytes", &workspace_bytes);
   ops.impl("fp64_emu_set_wait_limit_ns", &set_wait_limit_ns);
@@ -412,4 +423,5 @@ TORCH_LIBRARY_IMPL(fp64_emu_b200, CUDA, ops) {
   ops.impl("fp64_emu_host_submit", &host_submit);   // CPU operands, CUDA buffers: the CUDA key
   ops.impl("fp64_emu_status", &status);
   ops.impl("fp64_emu_debug_fetch", &debug_fetch);
+  ops.impl("fp64_emu_wait_selftest", &wait_selftest);
 }

@@ -160,6 +160,14 @@ F64E_API int f64e_status(const void* workspace, void* stream, int32_t* status);
  * 2e9).  Process-wide. */
 F64E_API void f64e_set_wait_limit_ns(uint64_t ns);
 
+/* Failure-detection self-test: one device thread waits, with the GEMM's
+ * bounded wait, on a barrier that nothing arrives at, so the wait runs out
+ * after limit_ns (0 < limit_ns <= 1e10) and records its site code (9) in the
+ * workspace status word; *status receives the word.  The context stays
+ * usable.  Synchronizes the stream.  Returns F64E_OK / F64E_ERR_*. */
+F64E_API int f64e_wait_selftest(void* workspace, size_t workspace_bytes, uint64_t limit_ns, void* stream,
+                                int32_t* status);
+
 /* Message of the last failed call on this thread ("" if none). */
 F64E_API const char* f64e_last_error(void);
 

@@ -352,3 +352,25 @@ def test_bitexact_vs_reference_nonfinite(emu, ref):
     mine = emu.mm(A, B).cpu().numpy()
     theirs = ref.mm(A, B).cpu().numpy()
     assert same_bits(mine, theirs)
+
+
+def test_bounded_wait_runs_out_and_reports(emu):
+    # failure detection without a fault: one device thread waits, through the
+    # GEMM's bounded wait, on a barrier that nothing arrives at; the wait runs
+    # out, its site code lands in the status word, and the context stays usable
+    import time
+    ws = torch.zeros(4096, dtype=torch.uint8, device="cuda")
+    t0 = time.perf_counter()
+    st = emu.ops.fp64_emu_wait_selftest(ws, 50_000_000)          # 50 ms
+    dt = time.perf_counter() - t0
+    assert st == 9
+    assert 0.04 < dt < 10.0
+    assert emu.ops.fp64_emu_status(ws) == 9
+    torch.manual_seed(21)
+    A = torch.randn(200, 300, dtype=torch.float64, device="cuda")
+    B = torch.randn(150, 300, dtype=torch.float64, device="cuda")
+    C = emu.mm(A, B)
+    torch.cuda.synchronize()
+    assert torch.allclose(C, A @ B.t(), rtol=1e-12, atol=1e-12)
+    with pytest.raises(RuntimeError):
+        emu.ops.fp64_emu_wait_selftest(ws, 0)

@@ -146,3 +146,48 @@ def test_host_share_ranges_partition_each_block(world, shape, b_kn):
         parts = sorted(host_share_ranges(r, world, M, N, K, b_kn)[1] for r in ranks)
         covered = [x for b0, b1 in parts for x in range(b0, b1)]
         assert covered == list(range(ext))
+
+
+def _failing_worker(rank, world, port, outdir):
+    # rank 1 leaves between steps (before its next collective); rank 0's next
+    # collective -- the MAX all-reduce of the sizing protocol -- must end with
+    # an error within the short process-group timeout instead of waiting
+    for p in (ROOT, os.path.join(ROOT, "fp64-emu_b200")):
+        if p not in sys.path:
+            sys.path.insert(0, p)
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    import time
+    from datetime import timedelta
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=5))
+    from fp64_emu import dist as proto_mod
+    maxlg = torch.zeros(2, dtype=torch.float32)
+    # one good step on both ranks
+    proto_mod.sized_protocol(lambda: maxlg.fill_(float(rank)), maxlg)
+    assert float(maxlg[0]) == world - 1
+    if rank == 1:
+        os._exit(3)                  # the rank dies between steps
+    t0 = time.perf_counter()
+    try:
+        proto_mod.sized_protocol(lambda: maxlg.fill_(0.0), maxlg)
+        outcome = "no error"
+    except Exception as e:  # noqa: BLE001
+        outcome = "error " + type(e).__name__
+    with open(os.path.join(outdir, "rank0.txt"), "w") as f:
+        f.write(f"{outcome} {time.perf_counter() - t0:.1f}")
+    os._exit(0)                      # no teardown collective with a dead peer
+
+
+def test_rank_failure_ends_the_next_collective_with_an_error(tmp_path):
+    port = _free_port()
+    ctx = mp.start_processes(_failing_worker, args=(2, port, str(tmp_path)), nprocs=2, join=False,
+                             start_method="spawn")
+    for p in ctx.processes:
+        p.join(120)
+    codes = [p.exitcode for p in ctx.processes]
+    for p in ctx.processes:
+        if p.is_alive():
+            p.kill()
+    assert codes == [0, 3]
+    outcome, secs = (tmp_path / "rank0.txt").read_text().rsplit(" ", 1)
+    assert outcome.startswith("error") and float(secs) < 60

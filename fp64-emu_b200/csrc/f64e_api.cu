@@ -822,8 +822,8 @@ int run(const f64e_problem* p, const double* A, const double* B, double* out, vo
   if (rc) return rc;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (l.MF == 0 || l.NF == 0) return F64E_OK;
-  if (!A || !B || !out) return fail(F64E_ERR_ARGUMENT, "null operand pointer");
-  if (l.K == 0) {
+  if (!out) return fail(F64E_ERR_ARGUMENT, "null output pointer");
+  if (l.K == 0) {   // empty inner dimension: C = 0 (the operands hold no elements, their pointers may be null)
     if (phases & F64E_PHASE_COMPUTE) {
       cudaError_t e = cudaMemsetAsync(out, 0, sizeof(double) * l.MF * l.N, s);
       if (e == cudaSuccess && out_host)
@@ -832,6 +832,7 @@ int run(const f64e_problem* p, const double* A, const double* B, double* out, vo
     }
     return F64E_OK;
   }
+  if (!A || !B) return fail(F64E_ERR_ARGUMENT, "null operand pointer");
   if (!ws || ws_bytes < l.total) return fail(F64E_ERR_WORKSPACE, "workspace of %zu bytes is below the %zu needed",
                                              ws_bytes, l.total);
   if (reinterpret_cast<uintptr_t>(ws) & 255) return fail(F64E_ERR_WORKSPACE, "workspace must be 256-byte aligned");

@@ -63,6 +63,9 @@ ORACLE_CASES = [
     ("mm_nt", 1, 64, 300, 50, "randn", {"exact": False}),
     ("mm_nt", 1, 96, 700, 80, "wide8", {"bits": 40}),
     ("mm_nt", 1, 1, 1, 1, "randn", {}),
+    ("mm_nt", 1, 33, 1, 20, "randn", {}),               # K = 1
+    ("mm", 1, 7, 1, 9, "wide16", {}),
+    ("bmm_nt", 2, 3, 1, 5, "randn", {}),
     ("mm", 1, 5, 17, 3, "randn", {"nprimes": 20}),
     ("bmm", 3, 100, 333, 77, "randn", {}),
     ("bmm_nt", 4, 40, 200, 30, "illcond", {}),
@@ -285,6 +288,11 @@ def test_empty_and_zero(emu):
     A = torch.zeros(0, 16, dtype=torch.float64, device="cuda")
     B = torch.randn(5, 16, dtype=torch.float64, device="cuda")
     assert emu.mm(A, B).shape == (0, 5)
+    # empty inner dimension: C = 0, as for torch.matmul
+    for kind, a, b in (("mm_nt", (4, 0), (0, 3)), ("mm", (4, 0), (3, 0)), ("bmm_nt", (2, 4, 0), (2, 0, 3))):
+        C = getattr(emu, kind)(torch.empty(a, dtype=torch.float64, device="cuda"),
+                               torch.empty(b, dtype=torch.float64, device="cuda"))
+        assert C.shape[-2:] == (4, 3) and not C.any()
     Z = torch.zeros(7, 9, dtype=torch.float64, device="cuda")
     assert torch.equal(emu.mm(Z, torch.zeros(3, 9, dtype=torch.float64, device="cuda")),
                        torch.zeros(7, 3, dtype=torch.float64, device="cuda"))

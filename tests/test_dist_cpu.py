@@ -191,3 +191,64 @@ def test_rank_failure_ends_the_next_collective_with_an_error(tmp_path):
     assert codes == [0, 3]
     outcome, secs = (tmp_path / "rank0.txt").read_text().rsplit(" ", 1)
     assert outcome.startswith("error") and float(secs) < 60
+
+
+def _lonely_worker(rank, world, port, outdir):
+    # rank 0 of a world of 2 whose peer never starts: the rendezvous must end
+    # with an error within its timeout instead of waiting for good
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    import time
+    from datetime import timedelta
+    t0 = time.perf_counter()
+    try:
+        dist.init_process_group("gloo", rank=0, world_size=2, timeout=timedelta(seconds=3))
+        outcome = "joined"
+    except Exception as e:  # noqa: BLE001
+        outcome = "error " + type(e).__name__
+    with open(os.path.join(outdir, "lonely.txt"), "w") as f:
+        f.write(f"{outcome} {time.perf_counter() - t0:.1f}")
+    os._exit(0)
+
+
+def test_rank_that_never_joins_ends_the_rendezvous_with_an_error(tmp_path):
+    port = _free_port()
+    ctx = mp.start_processes(_lonely_worker, args=(1, port, str(tmp_path)), nprocs=1, join=False,
+                             start_method="spawn")
+    ctx.processes[0].join(120)
+    if ctx.processes[0].is_alive():
+        ctx.processes[0].kill()
+    outcome, secs = (tmp_path / "lonely.txt").read_text().rsplit(" ", 1)
+    assert outcome.startswith("error") and float(secs) < 60
+
+
+def _mismatch_worker(rank, world, port, outdir):
+    # the ranks disagree on the collective's shape (one of them built a
+    # different product): the collective must fail on some rank, not hang
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    from datetime import timedelta
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=5))
+    t = torch.zeros(2 if rank == 0 else 3, dtype=torch.float32)
+    try:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        outcome = "no error"
+    except Exception as e:  # noqa: BLE001
+        outcome = "error " + type(e).__name__
+    with open(os.path.join(outdir, f"mismatch{rank}.txt"), "w") as f:
+        f.write(outcome)
+    os._exit(0)
+
+
+def test_mismatched_collective_shapes_end_with_an_error(tmp_path):
+    port = _free_port()
+    ctx = mp.start_processes(_mismatch_worker, args=(2, port, str(tmp_path)), nprocs=2, join=False,
+                             start_method="spawn")
+    for p in ctx.processes:
+        p.join(120)
+    for p in ctx.processes:
+        if p.is_alive():
+            p.kill()
+    outcomes = [(tmp_path / f"mismatch{r}.txt").read_text() for r in range(2)
+                if (tmp_path / f"mismatch{r}.txt").exists()]
+    assert outcomes and any(o.startswith("error") for o in outcomes)

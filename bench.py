@@ -19,7 +19,13 @@ the two sizing maxima; total work is fixed, so scaling is "strong".
           per launch / its average duration over the timed region
   accuracy  the metric's "correct bits vs dd": after timing, the product's
           first 256 rows (rank 0's block) against a double-double product,
-          with cuBLAS DGEMM on the same sample (fp64_emu.accuracy)
+          with cuBLAS DGEMM on the same sample (dd_accuracy, which imports
+          torch only)
+  output_sha256  SHA-256 of the same output sample's float64 bytes (both
+          arms print it; equal digests mean bit-identical products); at
+          N > 1 rank 0 also recomputes the whole product unpartitioned on one
+          GPU after timing and compares every rank's block digest with it
+          (blocks_bit_identical)
 
 --impl reference runs the reference's own CUDA kernels (the build in
 oracle/_ref, compiled from the reference sources; the reference has no CPU
@@ -27,6 +33,7 @@ implementation of this path) through its own Python API on one GPU, with
 the same workload and protocol; under torchrun only rank 0 runs it.
 """
 import argparse
+import hashlib
 import json
 import math
 import os
@@ -146,16 +153,43 @@ def make_inputs(dist_name, batch, M, N, K, nt, device, seed=0):
     return A, B
 
 
+INT8_PEAK_RECORD = os.path.join(ROOT, "profiles", "int8_peak_b200.md")
+
+
 def int8_peak_from_file():
-    """INT8 dense peak: B200's INT8 dense rate is twice its BF16 dense rate;
-    the BF16 figures are the pool's measured cuBLAS numbers."""
+    """Dense INT8 peak (TOPS): (sustained, burst, source).  The measured
+    cuBLAS INT8 GEMM rate on this pool (`bench.py --int8-peak`, committed in
+    profiles/int8_peak_b200.md) when that record exists; otherwise twice the
+    measured BF16 dense rate of MEASURED_PEAKS.json (B200's INT8 dense rate is
+    twice its BF16 one); otherwise the pool's fallback figures."""
+    vals = {}
+    try:
+        with open(INT8_PEAK_RECORD) as f:
+            for line in f:
+                line = line.strip().strip("`")
+                if line.startswith("int8_tops_") and "=" in line:
+                    k, v = line.split("=", 1)
+                    vals[k.strip()] = float(v.split()[0])
+        if "int8_tops_burst" in vals and "int8_tops_sustained" in vals:
+            return vals["int8_tops_sustained"], vals["int8_tops_burst"], "measured cuBLAS INT8 GEMM (torch._int_mm)"
+    except (OSError, ValueError, IndexError):
+        pass
     path = os.path.join(ROOT, "MEASURED_PEAKS.json")
     try:
         with open(path) as f:
             mp = json.load(f)
-        return 2.0 * float(mp["bf16_tflops_sustained"]), 2.0 * float(mp["bf16_tflops"]), "measured"
+        return 2.0 * float(mp["bf16_tflops_sustained"]), 2.0 * float(mp["bf16_tflops"]), "2 x measured bf16"
     except (OSError, KeyError, ValueError):
-        return 2.0 * 1400.0, 2.0 * 1590.0, "fallback"
+        return 2.0 * 1400.0, 2.0 * 1590.0, "2 x fallback bf16"
+
+
+def bf16_peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            mp = json.load(f)
+        return float(mp["bf16_tflops_sustained"]), float(mp["bf16_tflops"])
+    except (OSError, KeyError, ValueError):
+        return 1400.0, 1590.0
 
 
 def profiled_traffic_per_step():
@@ -169,6 +203,54 @@ def profiled_traffic_per_step():
     except (OSError, ValueError, IndexError):
         pass
     return None
+
+
+# ------------------------------------------------ workload / sample helpers --
+def grid_of(world):
+    """(row blocks, column blocks) of the 2-D partition of C for `world` ranks.
+    The same rule as fp64_emu.dist.grid_shape, restated so that the reference
+    arm imports nothing of this repository (tests/test_bench_cpu.py checks
+    that the two agree)."""
+    pr = 1
+    while (pr * 2) ** 2 <= world and world % (pr * 2) == 0:
+        pr *= 2
+    return pr, world // pr
+
+
+def first_block(n, parts):
+    """Length of block 0 when n splits into `parts` nearly equal blocks (as
+    fp64_emu.dist.block_range)."""
+    base, rem = divmod(n, parts)
+    return base + (1 if rem > 0 else 0)
+
+
+def workload_config(name):
+    """The `config` object of both arms: the workload only (same dict in the
+    reference arm and ours, whatever the partition)."""
+    kind, batch, M, N, K, dist_name, nprimes, corr = WORKLOADS[name]
+    plan = "default plan (plan_config(K))" if nprimes is None and corr is None else \
+        f"plan nprimes={nprimes} corr={corr}"
+    return {"workload": f"{name}: {kind} batch={batch} M={M} N={N} K={K} {dist_name}, {plan}",
+            "l2": "operands larger than L2 (no flush)"}
+
+
+def sample_region(name, world):
+    """(batch member or None, rows, columns) of the output sample that both
+    arms hash and measure: the first 256 rows of rank 0's block by all of the
+    block's columns (of batch member 0 for batches).  Rank 0's block starts at
+    row 0 and column 0, so in the full product the sample is C[:rows, :cols]."""
+    kind, batch, M, N, K = WORKLOADS[name][:5]
+    if batch > 1:
+        return 0, min(256, M), N
+    pr, pc = grid_of(world)
+    return None, min(256, first_block(M, pr)), first_block(N, pc)
+
+
+def sample_sha256(C, name, world):
+    """SHA-256 of the sample's float64 bytes (row-major)."""
+    b, R, Nc = sample_region(name, world)
+    X = C[b] if b is not None else C
+    return hashlib.sha256(X[:R, :Nc].contiguous().cpu().numpy().tobytes()).hexdigest()
 
 
 # ----------------------------------------------------------- our product --
@@ -451,10 +533,10 @@ def run_ours(args):
         "vs_baseline": None,
         "dtype": "f64",
         "data": "synthetic",
-        "config": {"workload": f"{args.workload}: {kind} batch={batch} M={M} N={N} K={K} {dist_name}, "
-                               f"plan nprimes={nprimes} corr={corr} ({G} INT8 GEMMs per product)",
-                   "parallelism": part, "l2": "operands larger than L2 (no flush)",
-                   "compute": "s8 x s8 -> s32 tcgen05 residue GEMMs, exact int128 recombine"},
+        "config": workload_config(args.workload),
+        "partition": part,
+        "plan": {"nprimes": nprimes, "corr": corr, "int8_gemms_per_product": G},
+        "compute": "s8 x s8 -> s32 tcgen05 residue GEMMs, exact int128 recombine",
         "e2e": {"value": round(work / (e2e_ms * 1e-3) / 1e12, 3), "unit": UNIT, "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h,
                 "api": ("fp64_emu.HostStream (operand copies, product and result copy of neighbouring steps "
@@ -466,10 +548,11 @@ def run_ours(args):
         "roofline": {"bound": "tensor", "kernel": "residue_gemm_pair_kernel" if Ml > 128 else "residue_gemm_tc_kernel",
                      "achieved": round(achieved, 1), "peak": round(peak, 1), "unit": "TOPS (int8)",
                      "frac": round(achieved / peak, 4),
-                     "peak_note": f"INT8 dense = 2 x measured bf16 dense ({src} MEASURED_PEAKS.json, "
-                                  f"{'burst: SM clock held' if held else 'sustained: SM clock sagged'}); "
-                                  f"nominal 8192 MAC/clk/SM at the sampled clock = {nominal:.0f} TOPS, "
-                                  f"frac of nominal {achieved / nominal:.3f}",
+                     "peak_note": f"INT8 dense peak of measured: {src}, "
+                                  f"{'burst (SM clock held)' if held else 'sustained (SM clock sagged)'}; "
+                                  f"for context 2 x measured bf16 dense = {2 * bf16_peaks()[1]:.0f} TOPS burst, "
+                                  f"nominal 8192 MAC/clk/SM at the sampled clock = {nominal:.0f} TOPS "
+                                  f"(frac of nominal {achieved / nominal:.3f})",
                      "gemm_ms_per_step": round(gemm_ms, 4), "traffic": traffic,
                      "per": "step: achieved over the step's GEMM busy time, traffic summed over its GEMM launches"},
         "phases_ms": {"gemm_busy": round(gemm_ms, 4), "outside_gemm": round(ms - gemm_ms, 4),
@@ -492,30 +575,82 @@ def run_ours(args):
         result["native_dgemm"] = native_dgemm(A_l, B_l, nt, args)
     if rank == 0 and not args.no_accuracy:
         try:
-            result["accuracy"] = accuracy_sample(kind, A_l, B_l, step.out,
+            result["accuracy"] = accuracy_sample(kind, A_l, B_l, step.out, args.workload, world,
                                                  others={"native_dgemm": lambda a, b: a @ b})
         except Exception as e:  # noqa: BLE001
             result["accuracy"] = {"error": str(e)[:200]}
     if rank == 0:
+        result["output_sha256"] = {"sample": sample_description(args.workload, world),
+                                   "value": sample_sha256(step.out, args.workload, world)}
+    if world > 1 and not args.no_block_check:
+        # every rank's block against the same block of the unpartitioned
+        # product, computed on rank 0's GPU after timing (collective: all ranks)
+        ok = check_blocks(args, step.out, rank, world, dev)
+        if rank == 0:
+            result["blocks_bit_identical"] = ok
+    if rank == 0:
         print(json.dumps(result), flush=True)
 
 
-def accuracy_sample(kind, A, B, C, others=None, rows=256):
-    """Correct bits against the double-double product (fp64_emu.accuracy)
-    on a sample: the first `rows` rows of the block (of batch member 0) by
-    every column.  `others`: name -> callable giving another product of the
-    same sample to measure alongside (cuBLAS DGEMM).  Runs after timing."""
-    from fp64_emu import accuracy as acc
+def sample_description(name, world):
+    b, R, Nc = sample_region(name, world)
+    return (f"C[{R} rows x {Nc} cols] at row 0, col 0" + (" of batch member 0" if b is not None else "")
+            + (f" (rank 0's block of {world})" if world > 1 else "") + ", float64 bytes row-major")
+
+
+def check_blocks(args, out, rank, world, dev):
+    """Digest of every rank's block, gathered; rank 0 recomputes the whole
+    product unpartitioned on its GPU (the public fp64_emu API) and compares
+    the same blocks.  True when every block is bit-identical."""
+    kind, batch, M, N, K, dist_name, nprimes, corr = WORKLOADS[args.workload]
+    nt = kind in ("mm_nt", "bmm_nt")
+    mine = hashlib.sha256(out.contiguous().cpu().numpy().tobytes()).digest()
+    d = torch.tensor(list(mine), dtype=torch.uint8, device=dev)
+    allg = torch.empty(world * 32, dtype=torch.uint8, device=dev)
+    dist.all_gather_into_tensor(allg, d)
+    if rank != 0:
+        return None
+    import fp64_emu
+    from fp64_emu.dist import block_range, rank_block
+    got = bytes(allg.cpu().tolist())
+    A, B = make_inputs(dist_name, batch, M, N, K, nt, dev, seed=args.seed)
+    kw = {k: v for k, v in (("nprimes", nprimes), ("corr", corr)) if v is not None}
+    C = getattr(fp64_emu, kind)(A, B, **kw)
+    del A, B
+    ok = True
+    for r in range(world):
+        if batch > 1:
+            b0, b1 = block_range(batch, world, r)
+            blk = C[b0:b1]
+        else:
+            (r0, r1), (c0, c1) = rank_block(r, world, M, N)
+            blk = C[r0:r1, c0:c1]
+        ok = ok and hashlib.sha256(blk.contiguous().cpu().numpy().tobytes()).digest() == got[32 * r:32 * r + 32]
+    del C
+    torch.cuda.empty_cache()
+    return ok
+
+
+def accuracy_sample(kind, A, B, C, name, world, others=None):
+    """Correct bits against the double-double product (dd_accuracy) on the
+    output sample of sample_region (the first 256 rows of rank 0's block by
+    the block's columns, of batch member 0): A, B and C are rank 0's block
+    operands and product (our arm) or the whole ones (reference arm; rank 0's
+    block starts at row 0 and column 0).  `others`: name -> callable giving
+    another product of the same sample to measure alongside (cuBLAS DGEMM).
+    Runs after timing."""
+    import dd_accuracy as acc
     nt = kind in ("mm_nt", "bmm_nt")
     batched = A.dim() == 3
     if batched:
         A, B, C = A[0], B[0], C[0]
-    R = min(rows, A.size(0))
+    _, R, Nc = sample_region(name, world)
     As = A[:R]
-    Bt = (B if nt else B.t()).contiguous()
+    Bt = (B[:, :Nc] if nt else B[:Nc].t()).contiguous()
+    C = C[:, :Nc]
     t0 = time.perf_counter()
     hi, lo = acc.dd_product(As, Bt)
-    res = {"sample": f"{R} rows x {Bt.size(1)} columns" + (" of batch member 0" if batched else ""),
+    res = {"sample": sample_description(name, world),
            "measure": "-log2(max|C - hi - lo| / max|hi|) against the double-double product (hi, lo); "
                       "element bits: -log2(|C - hi - lo| / |hi|), capped at 60",
            "value": acc.summary(C[:R], hi, lo)}
@@ -558,6 +693,7 @@ def load_reference():
 
 def run_reference(args):
     rank = dist.get_rank() if dist.is_initialized() else 0
+    world = dist.get_world_size() if dist.is_initialized() else 1
     if rank != 0:
         return
     R, why = load_reference()
@@ -614,22 +750,85 @@ def run_reference(args):
         "value": value, "unit": UNIT, "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
         "dtype": "f64", "data": "synthetic",
-        "config": {"workload": f"{args.workload}: {kind} batch={batch} M={M} N={N} K={K} {dist_name}, "
-                               f"reference default dispatch (first-call probe excluded)",
-                   "l2": "operands larger than L2 (no flush)"},
+        "config": workload_config(args.workload),
+        "impl_note": ("the reference's own CUDA build (oracle/_ref, compiled from its sources with its JIT recipe) "
+                      "through its Python API on one B200, " +
+                      (f"FP64EMU_PATH={os.environ['FP64EMU_PATH']}" if os.environ.get("FP64EMU_PATH")
+                       else "default dispatch") + ", first-call probe excluded; the reference has no CPU "
+                      "implementation of this path, so there is no cpu_baseline in this line"),
         "e2e": {"value": round(work / (e2e_ms * 1e-3) / 1e12, 3), "unit": UNIT,
                 "h2d_bytes_per_step": (A.numel() + B.numel()) * 8, "d2h_bytes_per_step": C0.numel() * 8},
-        "cpu_baseline": {"value": value, "unit": UNIT, "cores": 0, "kind": "reference",
-                         "sample": "the reference's own CUDA kernels (oracle/_ref, built from its sources) on "
-                                   "one B200: the reference has no CPU implementation of this path"},
+        "output_sha256": {"sample": sample_description(args.workload, world),
+                          "value": sample_sha256(C0, args.workload, world)},
         "clocks": clk,
     }
     if not args.no_accuracy:
         try:
-            result["accuracy"] = accuracy_sample(kind, A, B, C0)
+            result["accuracy"] = accuracy_sample(kind, A, B, C0, args.workload, world)
         except Exception as e:  # noqa: BLE001
             result["accuracy"] = {"error": str(e)[:200]}
     print(json.dumps(result), flush=True)
+
+
+# ------------------------------------------------------------ INT8 peak --
+def run_int8_peak(args):
+    """Dense INT8 GEMM peak of this B200 through cuBLAS (torch._int_mm, s8 x
+    s8 -> s32), n x n x n: the best of 10 back-to-back launches per operand
+    layout (burst), then the better layout back to back for about 4 s
+    (sustained), with the SM clock sampled throughout.  Prints one JSON line;
+    the figures recorded in profiles/int8_peak_b200.md are what bench.py
+    divides by."""
+    dev = torch.device("cuda", torch.cuda.current_device())
+    n = args.peak_n
+    g = torch.Generator(device=dev).manual_seed(0)
+    a = torch.randint(-128, 128, (n, n), dtype=torch.int8, device=dev, generator=g)
+    b_rm = torch.randint(-128, 128, (n, n), dtype=torch.int8, device=dev, generator=g)
+    b_cm = b_rm.t().contiguous().t()     # same values, column-major
+    ops = 2.0 * n * n * n
+    clocks = ClockSampler(dev)
+    clocks.start()
+    burst = {}
+    for name, b in (("b column-major", b_cm), ("b row-major", b_rm)):
+        try:
+            for _ in range(3):
+                torch._int_mm(a, b)
+            torch.cuda.synchronize()
+            best = float("inf")
+            for _ in range(10):
+                s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                s.record()
+                torch._int_mm(a, b)
+                e.record()
+                e.synchronize()
+                best = min(best, s.elapsed_time(e))
+            burst[name] = ops / (best * 1e-3) / 1e12
+        except RuntimeError as ex:   # a layout cuBLAS does not take
+            burst[name] = None
+            log(f"int8 peak: {name}: {ex}")
+    clk_burst = clocks.stop()
+    layout = max((k for k in burst if burst[k]), key=lambda k: burst[k])
+    b = b_cm if layout == "b column-major" else b_rm
+    clocks = ClockSampler(dev)
+    clocks.start()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    t0, k = time.perf_counter(), 0
+    while time.perf_counter() - t0 < args.peak_seconds:
+        for _ in range(20):
+            torch._int_mm(a, b)
+        k += 20
+        if k % 100 == 0:
+            torch.cuda.synchronize()
+    e.record()
+    torch.cuda.synchronize()
+    sustained = ops * k / (s.elapsed_time(e) * 1e-3) / 1e12
+    clk_sus = clocks.stop()
+    print(json.dumps({"int8_peak": {"n": n, "op": "torch._int_mm (cuBLAS), s8 x s8 -> s32",
+                                    "burst_tops": {k2: (round(v, 1) if v else None) for k2, v in burst.items()},
+                                    "layout": layout, "burst_best_tops": round(burst[layout], 1),
+                                    "sustained_tops": round(sustained, 1), "sustained_launches": k,
+                                    "clocks_burst": clk_burst, "clocks_sustained": clk_sus,
+                                    "gpu": torch.cuda.get_device_name(dev)}}), flush=True)
 
 
 def main():
@@ -645,6 +844,12 @@ def main():
     ap.add_argument("--no-native", action="store_true", help="skip the cuBLAS DGEMM context number")
     ap.add_argument("--no-accuracy", action="store_true",
                     help="skip the correct-bits measurement after timing (one small launch per K step)")
+    ap.add_argument("--no-block-check", action="store_true",
+                    help="N > 1: skip the unpartitioned recomputation that checks every rank's block")
+    ap.add_argument("--int8-peak", action="store_true",
+                    help="measure the dense INT8 GEMM peak (cuBLAS through torch._int_mm) and exit")
+    ap.add_argument("--peak-n", type=int, default=8192)
+    ap.add_argument("--peak-seconds", type=float, default=4.0)
     args = ap.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
@@ -655,7 +860,9 @@ def main():
         dist.init_process_group("nccl", timeout=timedelta(seconds=300),
                                 device_id=torch.device("cuda", local))
     try:
-        if args.impl == "reference":
+        if args.int8_peak:
+            run_int8_peak(args)
+        elif args.impl == "reference":
             run_reference(args)
         else:
             run_ours(args)

@@ -142,6 +142,18 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint64
   }
 }
 
+// Limit of the teardown waits (copies and MMAs a CTA issued, before it frees
+// TMEM or exits).  Never shorter than kDrainFloorNs, whatever the caller's
+// wait limit: a short limit may end a main-loop wait on a device that is only
+// slow (time-sliced with another context), and the in-flight work must still
+// land before its shared memory and TMEM are released.  Only a device that has
+// stopped making progress runs this out.
+constexpr uint64_t kDrainFloorNs = 4000000000ull;  // 4 s
+
+__device__ __forceinline__ uint64_t drain_limit(uint64_t limit_ns) {
+  return limit_ns > kDrainFloorNs ? limit_ns : kDrainFloorNs;
+}
+
 // -------------------------------------------------------------------- TMA --
 // Tiled 3-D load, no multicast: box lands in this CTA's shared memory and
 // completes `bytes` on the CTA's own mbarrier.
@@ -258,6 +270,16 @@ __device__ __forceinline__ void mbar_arrive_expect_tx_cluster(uint32_t cluster_a
   asm volatile("mbarrier.arrive.expect_tx.release.cluster.shared::cluster.b64 _, [%0], %1;" ::"r"(cluster_addr),
                "r"(bytes)
                : "memory");
+}
+// complete-tx of `bytes` on this CTA's mbarrier without a copy: stands in for
+// bytes a copy that was never issued would have delivered (teardown only).
+__device__ __forceinline__ void mbar_complete_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.complete_tx.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+// Store to a 32-bit shared variable of another CTA of the cluster (its
+// shared::cluster address); ordered for the reader by a cluster barrier.
+__device__ __forceinline__ void st_cluster_u32(uint32_t cluster_addr, uint32_t v) {
+  asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(cluster_addr), "r"(v) : "memory");
 }
 // Tiled 3-D load into this CTA's shared memory whose completion is counted on
 // an mbarrier of either CTA of the pair (no multicast).

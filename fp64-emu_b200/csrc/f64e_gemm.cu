@@ -20,7 +20,12 @@
 //               256-column accumulators and commits stages / tiles.
 //   warps 2..5  epilogue: tcgen05.ld 32 lanes x 32 columns, Barrett, store.
 // Every mbarrier wait is bounded; a timeout records its site in the status
-// word and the CTA unwinds (draining its copies and MMAs, freeing TMEM).
+// word and the CTA unwinds: it drains its copies and MMAs (teardown waits of
+// at least kDrainFloorNs, whatever the caller's limit), then frees TMEM.
+// In the CTA pair, the leader's drain covers both CTAs' copies (its full
+// barriers count the bytes of both) and every MMA (only the leader issues
+// them); the final cluster barrier keeps the peer from freeing its TMEM
+// columns or exiting before the leader's drain has ended.
 #include <map>
 #include <mutex>
 #include <set>
@@ -167,7 +172,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       // Drain: every copy this thread issued has landed before the CTA exits.
       const uint32_t first = j > (uint32_t)STAGES ? j - STAGES : 0;
       for (uint32_t jj = first; jj < j; jj++)
-        mbar_wait(&full_bar[jj % STAGES], (jj / STAGES) & 1, lim, g.status, kWaitDrain);
+        mbar_wait(&full_bar[jj % STAGES], (jj / STAGES) & 1, drain_limit(lim), g.status, kWaitDrain);
     }
   } else if (warp == 1) {
     // --------------------------------------------------------- MMA issuer --
@@ -202,7 +207,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       }
       // Drain: all MMAs issued by this thread complete before TMEM is freed.
       tc_commit(drain_bar);
-      mbar_wait(drain_bar, 0, lim, g.status, kWaitDrain);
+      mbar_wait(drain_bar, 0, drain_limit(lim), g.status, kWaitDrain);
     }
   } else {
     // ----------------------------------------------------------- epilogue --
@@ -303,6 +308,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   uint64_t* drain_bar = acc_empty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  volatile uint32_t* peer_issued = reinterpret_cast<volatile uint32_t*>(tmem_slot + 2);  // leader: peer's stage count
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = cluster_ctarank();
@@ -321,6 +327,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
     mbar_init(drain_bar, 1);
     *abort_flag = 0;
+    *peer_issued = 0;
     fence_barrier_init();
     tma_prefetch_desc(&tmapA);
     tma_prefetch_desc(&tmapB);
@@ -339,9 +346,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   const uint32_t full0 = mapa_shared(smem_u32(&full_bar[0]), 0);     // leader's full barriers
   const uint32_t accempty0 = mapa_shared(smem_u32(&acc_empty[0]), 0);  // leader's accumulator-empty
 
+  uint32_t issued = 0;    // stages this CTA's producer thread issued
+  bool producer = false;  // this thread is that producer
   if (warp == 0) {
     // ---------------------------------------------------------- producer --
-    if (elect_one()) {
+    producer = elect_one();
+    if (producer) {
       uint32_t j = 0;
       bool ok = true;
       for (int tile = cluster; tile < ntiles && ok; tile += nclusters) {
@@ -361,13 +371,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           tma_load_3d_pair(sB + s * PB_BYTES, &tmapB, kx, tl.n0 + PHALF * (int)rank, z, full0 + 8 * s);
         }
       }
-      // Drain: the leader's full barriers count both CTAs' bytes, so once they
-      // complete every copy of the pair has landed.
-      if (leader) {
-        const uint32_t first = j > (uint32_t)PSTAGES ? j - PSTAGES : 0;
-        for (uint32_t jj = first; jj < j; jj++)
-          mbar_wait(&full_bar[jj % PSTAGES], (jj / PSTAGES) & 1, lim, g.status, kWaitDrain);
-      }
+      issued = j;
+      // The leader drains the copies of both CTAs (its full barriers count
+      // both halves) after the first cluster barrier below; it needs the
+      // peer's count, which may differ from its own by up to PSTAGES stages
+      // when a wait ran out.
+      if (!leader) st_cluster_u32(mapa_shared(smem_u32((const void*)peer_issued), 0), j);
     }
   } else if (warp == 1) {
     // --------------------------------------------------------- MMA issuer --
@@ -401,7 +410,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         if (ok) tc_commit_pair(&acc_full[a], 0x3);
       }
       tc_commit_pair(drain_bar, 0x1);
-      mbar_wait(drain_bar, 0, lim, g.status, kWaitDrain);
+      mbar_wait(drain_bar, 0, drain_limit(lim), g.status, kWaitDrain);
     }
   } else {
     // ----------------------------------------------------------- epilogue --
@@ -464,6 +473,26 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   }
 
   tc_fence_before();
+  __syncwarp();
+  cluster_sync();   // the peer's stage count is visible; the leader's MMAs have drained
+  if (producer && leader) {
+    // Every copy of the pair lands before either CTA releases its shared
+    // memory.  Both producers issue a stage only after the MMAs that freed it
+    // completed, so neither runs more than PSTAGES stages ahead of the other
+    // and every stage older than the last PSTAGES issued by either is complete.
+    // A stage only the peer issued gets the leader's missing arrival (for the
+    // peer's half of the bytes); a stage only the leader issued gets the
+    // peer's half of the bytes as a complete-tx, since that copy never comes.
+    const uint32_t jp = *peer_issued;
+    const uint32_t jmax = issued > jp ? issued : jp;
+    const uint32_t lo = jmax > (uint32_t)PSTAGES ? jmax - PSTAGES : 0;
+    for (uint32_t jj = lo; jj < jmax; jj++) {
+      const uint32_t s = jj % PSTAGES;
+      if (jj >= issued) mbar_arrive_expect_tx(&full_bar[s], PSTAGE_BYTES);
+      else if (jj >= jp) mbar_complete_tx(&full_bar[s], PSTAGE_BYTES);
+      mbar_wait(&full_bar[s], (jj / PSTAGES) & 1, drain_limit(lim), g.status, kWaitDrain);
+    }
+  }
   __syncwarp();
   cluster_sync();
   if (warp == 1) {

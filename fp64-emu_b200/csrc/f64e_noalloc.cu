@@ -11,8 +11,12 @@
 // and a stream, and nothing is allocated.
 //
 // Limits and sharing:
-//   * the array occupies F64E_NOALLOC_SCRATCH_BYTES on every GPU where this
-//     entry point has been used, until the process exits;
+//   * the array occupies F64E_NOALLOC_SCRATCH_BYTES on every GPU whose
+//     context loads this library's device code: with CUDA's default lazy
+//     module loading that is every GPU where this entry point (or another
+//     kernel of the library) has run; with CUDA_MODULE_LOADING=EAGER it is
+//     every GPU the process creates a context on.  It is held until the
+//     context is destroyed (process exit or cudaDeviceReset);
 //   * problems whose workspace exceeds it are rejected (F64E_ERR_WORKSPACE);
 //   * every call on a device uses the same array, which keeps whatever the
 //     last call left there; calls whose work overlaps on the GPU (different
@@ -21,9 +25,12 @@
 //     writes every scratch byte it reads before reading it, and it clears
 //     its status word itself.
 //   * the array's host-side name is only a stand-in for the device copy, so
-//     the first call on each device looks up the device address with
-//     cudaGetSymbolAddress (with that device current) and caches it; that
-//     first call should come before any stream capture.
+//     the entry point looks up the device address with cudaGetSymbolAddress
+//     (with the caller's device current) the first time it runs in a CUDA
+//     context, and caches it under that context's unique id (cuCtxGetId):
+//     a new context -- after cudaDeviceReset, or a context the caller made
+//     with cuCtxCreate -- gets a fresh lookup instead of a stale address.
+//     That first call in a context should come before any stream capture.
 #include <mutex>
 
 #include "f64e.h"
@@ -41,24 +48,60 @@ static __device__ __align__(256) unsigned char g_noalloc_scratch[F64E_NOALLOC_SC
 
 constexpr int kMaxDevices = 64;
 std::mutex g_scratch_mtx;
-void* g_scratch_addr[kMaxDevices];  // device address of the array, per device; null until set up
+struct ScratchSlot {
+  unsigned long long ctx_id;  // unique id of the context the address belongs to
+  void* addr;                 // device address of the array there; null until set up
+};
+ScratchSlot g_scratch[kMaxDevices];
 
-// Device address of the scratch array on the current device (set up once per
-// device, with that device current).
+using CtxGetCurrentFn = CUresult (*)(CUcontext*);
+using CtxGetIdFn = CUresult (*)(CUcontext, unsigned long long*);
+
+// Unique id of the current CUDA context (driver entry points fetched through
+// the runtime, so the library links no libcuda).  0 when unavailable or when
+// no context is current yet (cudaGetSymbolAddress then creates the device's
+// primary context, and the next call caches under its id).
+unsigned long long current_context_id() {
+  static CtxGetCurrentFn get_current = nullptr;
+  static CtxGetIdFn get_id = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult qr;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &f, cudaEnableDefault, &qr) == cudaSuccess &&
+        qr == cudaDriverEntryPointSuccess)
+      get_current = reinterpret_cast<CtxGetCurrentFn>(f);
+    f = nullptr;
+    if (cudaGetDriverEntryPoint("cuCtxGetId", &f, cudaEnableDefault, &qr) == cudaSuccess &&
+        qr == cudaDriverEntryPointSuccess)
+      get_id = reinterpret_cast<CtxGetIdFn>(f);
+  });
+  CUcontext ctx = nullptr;
+  unsigned long long id = 0;
+  if (!get_current || !get_id || get_current(&ctx) != CUDA_SUCCESS || !ctx || get_id(ctx, &id) != CUDA_SUCCESS)
+    return 0;
+  return id;
+}
+
+// Device address of the scratch array in the current device's current
+// context (looked up once per context, with that device current).
 int scratch_address(void** out) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return f64e::report_error(F64E_ERR_CUDA, cudaGetErrorString(e));
   if (dev < 0 || dev >= kMaxDevices) return f64e::report_error(F64E_ERR_UNSUPPORTED, "device index out of range");
+  const unsigned long long ctx = current_context_id();
   std::lock_guard<std::mutex> lk(g_scratch_mtx);
-  if (!g_scratch_addr[dev]) {
+  ScratchSlot& s = g_scratch[dev];
+  if (!s.addr || ctx == 0 || s.ctx_id != ctx) {
     void* p = nullptr;
     e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
     if (e != cudaSuccess || !p)
       return f64e::report_error(F64E_ERR_CUDA, "cudaGetSymbolAddress of the no-alloc scratch failed");
-    g_scratch_addr[dev] = p;
+    s.addr = p;
+    s.ctx_id = ctx;
   }
-  *out = g_scratch_addr[dev];
+  *out = s.addr;
   return F64E_OK;
 }
 

@@ -1,5 +1,7 @@
 """Accuracy of a float64 product against a double-double one (measurement
-tooling, not on the product path).
+tooling, not on the product path).  Standalone: it imports torch only, never
+the fp64_emu package, so measuring another implementation's product with it
+loads none of this repository's libraries.
 
 dd_product(A, Bt) accumulates every inner product of A [R, K] and Bt [K, N]
 in double-double: Dekker's two-product (Veltkamp splitting, no fused

@@ -205,14 +205,18 @@ F64E_API int f64e_debug_fetch(const f64e_problem* p, const void* workspace, int 
  * not call cudaMalloc / cudaFree, sandboxed deployments without an allocator).
  * No counterpart in the reference.  Same arguments and result as f64e_mm_nt,
  * minus the workspace: the product runs in a file-scope device array of
- * F64E_NOALLOC_SCRATCH_BYTES, held on every GPU where this entry point has
- * been used until the process exits.  Problems needing more scratch are
- * rejected with F64E_ERR_WORKSPACE.  Nothing is allocated.  All calls on a
- * device share the one array (it keeps the last call's contents; nothing in
- * it needs to start at zero): calls whose work overlaps on the GPU race and
- * must be serialized by the caller.  The first call on each device looks up
- * the array's device address (cudaGetSymbolAddress) and should come before
- * any stream capture. */
+ * F64E_NOALLOC_SCRATCH_BYTES, held until the process exits on every GPU whose
+ * context loaded this library's device code -- under CUDA's default lazy
+ * module loading, the GPUs where the library has run a kernel; with
+ * CUDA_MODULE_LOADING=EAGER, every GPU the process opens.  Problems needing
+ * more scratch are rejected with F64E_ERR_WORKSPACE.  Nothing is allocated.
+ * All calls on a device share the one array (it keeps the last call's
+ * contents; nothing in it needs to start at zero): calls whose work overlaps
+ * on the GPU race and must be serialized by the caller.  The first call in
+ * each CUDA context looks up the array's device address
+ * (cudaGetSymbolAddress, cached under the context's id, so a reset or a
+ * caller-made context gets a fresh lookup) and should come before any
+ * stream capture. */
 F64E_API int f64e_mm_nt_noalloc(double* out, const double* A, const double* Bt, int64_t M, int64_t N, int64_t K,
                                 const int32_t* primes, int32_t nprimes, int32_t exact, int64_t bits,
                                 int32_t use_corr, void* stream);

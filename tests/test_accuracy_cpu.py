@@ -1,4 +1,4 @@
-"""fp64_emu.accuracy (the double-double measure bench.py reports): the torch
+"""dd_accuracy (the double-double measure bench.py reports): the torch
 form equals the numpy double-double of the test helpers bit for bit, is exact
 on exactly representable sums, and the bit measures read as defined."""
 import math
@@ -14,8 +14,8 @@ from helpers import correct_bits as np_correct_bits, dd_matmul, make  # noqa: E4
 
 @pytest.fixture(scope="module")
 def acc():
-    from fp64_emu import accuracy
-    return accuracy
+    import dd_accuracy
+    return dd_accuracy
 
 
 @pytest.mark.parametrize("dist", ["randn", "wide16", "illcond40"])
@@ -76,7 +76,8 @@ def test_bench_accuracy_sample_layouts(kind):
         A = torch.randn(40, 64, dtype=torch.float64, generator=g)
         B = torch.randn((64, 24) if nt else (24, 64), dtype=torch.float64, generator=g)
         C = A @ (B if nt else B.t())
-    r = bench.accuracy_sample(kind, A, B, C, others={"again": lambda a, b: a @ b}, rows=16)
-    assert r["sample"].startswith("16 rows x 24 columns")
+    name = "C5" if kind.startswith("bmm") else "C1"   # sample: the first 256 / 128 rows, all columns here
+    r = bench.accuracy_sample(kind, A, B, C, name, 1, others={"again": lambda a, b: a @ b})
+    assert r["sample"].startswith("C[")
     assert 45.0 < r["value"]["correct_bits"] <= 53.0
     assert r["again"]["correct_bits"] == pytest.approx(r["value"]["correct_bits"], abs=3.0)

@@ -57,20 +57,49 @@ def _with_workspace(L, A, Bt, primes, stream):
     return out
 
 
+def _noalloc(L, A, Bt, primes, stream, M, N, K):
+    got = torch.full((M, N), float("nan"), dtype=torch.float64, device="cuda")
+    rc = L.f64e_mm_nt_noalloc(got.data_ptr(), A.data_ptr() if A.numel() else None,
+                              Bt.data_ptr() if Bt.numel() else None, M, N, K, primes, len(PRIMES), 1, 53, 1, stream)
+    assert rc == 0, L.f64e_last_error()
+    torch.cuda.synchronize()
+    return got
+
+
 def test_noalloc_matches_workspace_entry_twice(lib):
     primes = (ctypes.c_int32 * len(PRIMES))(*PRIMES)
     stream = torch.cuda.current_stream().cuda_stream
     g = torch.Generator(device="cuda").manual_seed(77)
-    for M, K, N in ((384, 900, 200), (513, 1024, 511)):   # two calls in a row, different shapes
+    # two calls in a row, different shapes: the full-K call fills the array
+    # first, so the ragged-K call after it runs on the stale bytes the first
+    # one left (padding columns up to the next multiple of 16 included)
+    for M, K, N in ((513, 1024, 511), (384, 900, 200)):
         A = torch.randn(M, K, dtype=torch.float64, device="cuda", generator=g)
         Bt = torch.randn(K, N, dtype=torch.float64, device="cuda", generator=g) * 2.0 ** 9
         want = _with_workspace(lib, A, Bt, primes, stream)
-        got = torch.full((M, N), float("nan"), dtype=torch.float64, device="cuda")
-        rc = lib.f64e_mm_nt_noalloc(got.data_ptr(), A.data_ptr(), Bt.data_ptr(), M, N, K, primes, len(PRIMES), 1,
-                                    53, 1, stream)
-        assert rc == 0, lib.f64e_last_error()
-        torch.cuda.synchronize()
+        got = _noalloc(lib, A, Bt, primes, stream, M, N, K)
         assert torch.equal(got, want)
+
+
+def test_noalloc_tall_product_takes_the_chunked_path(lib):
+    # M >= 2048 with small N and K fits the array and runs the library's
+    # chunked pipeline (its own streams) on the shared scratch
+    primes = (ctypes.c_int32 * len(PRIMES))(*PRIMES)
+    stream = torch.cuda.current_stream().cuda_stream
+    g = torch.Generator(device="cuda").manual_seed(78)
+    M, K, N = 2048, 16, 16
+    A = torch.randn(M, K, dtype=torch.float64, device="cuda", generator=g)
+    Bt = torch.randn(K, N, dtype=torch.float64, device="cuda", generator=g)
+    want = _with_workspace(lib, A, Bt, primes, stream)
+    assert torch.equal(_noalloc(lib, A, Bt, primes, stream, M, N, K), want)
+
+
+def test_noalloc_empty_inner_dimension_gives_zeros(lib):
+    primes = (ctypes.c_int32 * len(PRIMES))(*PRIMES)
+    stream = torch.cuda.current_stream().cuda_stream
+    e = torch.empty(0, dtype=torch.float64, device="cuda")
+    got = _noalloc(lib, e, e, primes, stream, 7, 5, 0)
+    assert torch.equal(got, torch.zeros(7, 5, dtype=torch.float64, device="cuda"))
 
 
 def test_noalloc_rejects_problems_beyond_its_scratch(lib):

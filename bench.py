@@ -65,6 +65,10 @@ WORKLOADS = {
     "C5": ("bmm_nt", 64, 1024, 1024, 1024, "unif", None, None),
     # profiling case: same kernels as C2 at a quarter of the device footprint
     "P4096": ("mm_nt", 1, 4096, 4096, 4096, "randn", None, None),
+    # one rank's block of C2 / C4 on eight GPUs (2 x 4 grid), alone on one GPU:
+    # the per-rank timeline of the scaling runs
+    "C2blk8": ("mm_nt", 1, 4096, 2048, 8192, "randn", None, None),
+    "C4blk8": ("mm_nt", 1, 8192, 4096, 16384, "wide30", None, None),
 }
 
 
@@ -296,6 +300,18 @@ class Step:
                                                      sp.corr, 14, sp.slab_cols, [e.cuda_event for e in events[1:]])
 
     @staticmethod
+    def timeline(events, launches, step_ms):
+        """(head, gaps, tail) of one step in ms: from the step's start to its
+        first GEMM launch, the time between its first GEMM start and last GEMM
+        end when no GEMM ran, and from the last GEMM end to the step's end."""
+        t0 = events[0]
+        iv = [(t0.elapsed_time(events[1 + 2 * i]), t0.elapsed_time(events[2 + 2 * i])) for i in range(launches)]
+        if not iv:
+            return 0.0, 0.0, step_ms
+        first, last = min(a for a, _ in iv), max(b for _, b in iv)
+        return first, (last - first) - Step.gemm_ms(events, launches), step_ms - last
+
+    @staticmethod
     def gemm_ms(events, launches):
         """Time during which at least one GEMM launch of the step ran (chunks on
         two streams overlap at their boundaries)."""
@@ -445,6 +461,10 @@ def run_ours(args):
     barrier()
     ms_local = t_start.elapsed_time(t_stop) / args.steps
     gemm_ms_local = sum(Step.gemm_ms(ev[i], launches[i]) for i in range(args.steps)) / args.steps
+    # per-step timeline: each step ends where the next one starts
+    ends = [ev[i + 1][0] for i in range(args.steps - 1)] + [t_stop]
+    tl = [Step.timeline(ev[i], launches[i], ev[i][0].elapsed_time(ends[i])) for i in range(args.steps)]
+    head_local, gaps_local, tail_local = (sum(x[k] for x in tl) / args.steps for k in range(3))
 
     # e2e through the public API with host buffers.
     import fp64_emu
@@ -556,6 +576,11 @@ def run_ours(args):
                      "gemm_ms_per_step": round(gemm_ms, 4), "traffic": traffic,
                      "per": "step: achieved over the step's GEMM busy time, traffic summed over its GEMM launches"},
         "phases_ms": {"gemm_busy": round(gemm_ms, 4), "outside_gemm": round(ms - gemm_ms, 4),
+                      "head": round(max_over_ranks(head_local), 4), "gaps": round(max_over_ranks(gaps_local), 4),
+                      "tail": round(max_over_ranks(tail_local), 4),
+                      "rank0": {"head": round(head_local, 4), "gaps": round(gaps_local, 4),
+                                "tail": round(tail_local, 4), "gemm_busy": round(gemm_ms_local, 4),
+                                "ms_per_step": round(ms_local, 4)},
                       "gemm_launches_per_step": launches[-1] if launches else 0},
         "clocks": clk,
     }

@@ -559,7 +559,7 @@ int run_gemm(const Plan& l, const ModTables& T, const View& v, void* ws, const D
 }
 
 void run_reconstruct(const Plan& l, const ModTables& T, const View& v, void* ws, int corr_mode, const void* corr,
-                     cudaStream_t s, bool beside_gemm = false) {
+                     cudaStream_t s, bool beside_gemm = false, int sms = 0) {
   ReconArgs r{};
   r.res = v.res;
   r.corr_mode = corr_mode;
@@ -575,7 +575,7 @@ void run_reconstruct(const Plan& l, const ModTables& T, const View& v, void* ws,
   r.exact = l.exact;
   r.C = v.C;
   r.ldc = v.ldc;
-  launch_reconstruct(r, T, s, beside_gemm);
+  launch_reconstruct(r, T, s, beside_gemm, sms);
 }
 
 // Device-to-host copy of one view's block of C (rows of pitch ldc) to the
@@ -793,7 +793,7 @@ int run_pipelined(const Plan& l, const ModTables& T, const View& f, void* ws, co
   for (int u = 0; u < U; u++) {
     cudaStreamWaitEvent(s, E[e_gemm + u], 0);   // joins both GEMM streams
     // row chunks of a single product: every reconstruction but the last runs beside a GEMM chunk
-    run_reconstruct(l, T, units[u], ws, l.recon_corr, units[u].corr, s, !ch.by_batch && u + 1 < U);
+    run_reconstruct(l, T, units[u], ws, l.recon_corr, units[u].corr, s, !ch.by_batch && u + 1 < U, d.sms);
     if (out_host) {   // this block's copy to the host overlaps the later blocks' work
       cudaEventRecord(E[e_done + u], s);
       cudaStreamWaitEvent(pr->cp, E[e_done + u], 0);

@@ -105,6 +105,7 @@ struct ReconArgs {
 };
 // beside_gemm: the launch runs beside a resident GEMM chunk (picks the form
 // that takes less from it).
-void launch_reconstruct(const ReconArgs& a, const ModTables& T, cudaStream_t s, bool beside_gemm = false);
+void launch_reconstruct(const ReconArgs& a, const ModTables& T, cudaStream_t s, bool beside_gemm = false,
+                        int sms = 0);
 
 }  // namespace f64e

@@ -15,6 +15,11 @@
 #include <cstdlib>
 #include <cstring>
 
+#include <map>
+#include <mutex>
+#include <vector>
+
+#include "f64e_crt64.cuh"
 #include "f64e_device.cuh"
 #include "f64e_kernels.h"
 
@@ -437,20 +442,154 @@ __global__ void __launch_bounds__(256, 4) reconstruct_crt_kernel(const ReconArgs
 }
 
 
-void launch_reconstruct(const ReconArgs& a, const ModTables& T, cudaStream_t s, bool beside_gemm) {
+// FP64-pipe CRT form (exact mode, M < 2^120; f64e_crt64.cuh): the limb sums
+// sum_t u_t e_{t,l} as fused multiply-adds of exact doubles.  u_t * 2^32 is
+// built from the stored byte without a conversion: one byte_perm places the
+// byte, top bit flipped (u_t = r_t + 128), under the exponent of 2^52, and
+// subtracting 2^52 leaves u_t * 2^32 exactly.  Block (64, 4): x spans 64
+// four-column chunks of a row, y four rows; each thread reads one 32-bit word
+// (four columns) per residue plane.
+template <int CM, int MINB>
+__global__ void __launch_bounds__(256, MINB) reconstruct_f64_kernel(const ReconArgs a, const Crt64Tables T) {
+  const Gain gn = pick_gain(a.maxlg[0], a.maxlg[1], T.log2M, a.bits);
+  const double csc = crt64_pow2(gn.bits_eff - 15 - 40);
+  const int P = T.P;
+  const int64_t nq = (a.N + 3) >> 2;
+  const int64_t plane = a.MF * a.ldn;
+  const bool vec_out = ((a.ldc & 3) == 0) && ((reinterpret_cast<uintptr_t>(a.C) & 15) == 0);
+  for (int64_t i = (int64_t)blockIdx.y * 4 + threadIdx.y; i < a.MF; i += (int64_t)gridDim.y * 4) {
+    const int sa = (int)a.sftA[i] + gn.g;
+    const int16_t* __restrict__ sB = a.sftB + (a.M == a.MF ? 0 : (i / a.M) * a.N);
+    for (int64_t jq = (int64_t)blockIdx.x * 64 + threadIdx.x; jq < nq; jq += (int64_t)gridDim.x * 64) {
+      const int64_t j0 = jq << 2;
+      const int64_t off = i * a.ldn + j0;
+      uint32_t rw[kMaxP];
+#pragma unroll
+      for (int t = 0; t < kMaxP; t++)
+        rw[t] = (t < P) ? __ldg(reinterpret_cast<const unsigned int*>(a.res + t * plane + off)) : 0u;
+#pragma unroll
+      for (int t = 0; t < kMaxP; t++) rw[t] ^= 0x80808080u;   // u_t = r_t + 128 per byte
+      int64_t cr[4];
+      load_corr<CM>(a, off, plane, cr);
+      double outv[4];
+      uint32_t slow = 0;
+#pragma unroll
+      for (int e = 0; e < 4; e++) {
+        double a0 = T.z[0], a1 = T.z[1], a2 = T.z[2];
+#pragma unroll
+        for (int t = 0; t < kMaxP; t++) {
+          if (t >= P) break;
+          const double du = __hiloint2double((int)__byte_perm(rw[t], 0x43300000u, 0x7650u | (uint32_t)e), 0) - 0x1p52;
+          a0 = fma(du, T.e[t][0], a0);
+          a1 = fma(du, T.e[t][1], a1);
+          a2 = fma(du, T.e[t][2], a2);
+        }
+        const int64_t j = j0 + e;
+        const int sh = -sa - (j < a.N ? (int)sB[j] + gn.g : 0);
+        double r;
+        if (!crt64_finish_fast(T, a0, a1, a2, (double)cr[e], csc, sh, &r)) slow |= 1u << e;
+        outv[e] = r;
+      }
+      double* crow = a.C + i * a.ldc;
+      if (vec_out && j0 + 4 <= a.N) {
+        *reinterpret_cast<double2*>(crow + j0) = make_double2(outv[0], outv[1]);
+        *reinterpret_cast<double2*>(crow + j0 + 2) = make_double2(outv[2], outv[3]);
+      } else {
+#pragma unroll
+        for (int e = 0; e < 4; e++)
+          if (j0 + e < a.N) crow[j0 + e] = outv[e];
+      }
+      if (slow) {
+        // Rare: a quotient estimate near a tie, or a result that is zero,
+        // subnormal or overflows.  Recompute those elements with the exact
+        // tie check and ldexp's rounding, from the residues in memory, and
+        // overwrite what the common path stored for them.
+#pragma unroll 1
+        for (int e = 0; e < 4; e++) {
+          if (!((slow >> e) & 1) || j0 + e >= a.N) continue;
+          double a0 = T.z[0], a1 = T.z[1], a2 = T.z[2];
+#pragma unroll 1
+          for (int t = 0; t < P; t++) {
+            const double du = (double)((uint32_t)(uint8_t)a.res[t * plane + off + e] ^ 0x80u) * 0x1p32;
+            a0 = fma(du, T.e[t][0], a0);
+            a1 = fma(du, T.e[t][1], a1);
+            a2 = fma(du, T.e[t][2], a2);
+          }
+          const int sh = -sa - ((int)sB[j0 + e] + gn.g);
+          const int64_t ce = e == 0 ? cr[0] : (e == 1 ? cr[1] : (e == 2 ? cr[2] : cr[3]));
+          crow[j0 + e] = crt64_finish(T, a0, a1, a2, (double)ce, csc, sh);
+        }
+      }
+    }
+  }
+}
+
+// Tables of the FP64 CRT form for a modulus set, built once per set.
+const Crt64Tables& crt64_tables(const ModTables& T) {
+  static std::mutex mtx;
+  static std::map<std::vector<int32_t>, Crt64Tables> cache;
+  std::vector<int32_t> key(T.p, T.p + T.P);
+  std::lock_guard<std::mutex> lk(mtx);
+  auto it = cache.find(key);
+  if (it == cache.end()) {
+    Crt64Tables C;
+    crt64_build(key.data(), T.P, T.log2M, &C);
+    it = cache.emplace(key, C).first;
+  }
+  return it->second;
+}
+
+
+void launch_reconstruct(const ReconArgs& a, const ModTables& T, cudaStream_t s, bool beside_gemm, int sms) {
   if (a.MF <= 0 || a.N <= 0) return;
   const int64_t nq = (a.N + 3) >> 2;
-  const dim3 grid((unsigned)std::min<int64_t>((nq + 63) / 64, 1 << 20),
-                  (unsigned)std::min<int64_t>((a.MF + 3) / 4, 65535));
+  dim3 grid((unsigned)std::min<int64_t>((nq + 63) / 64, 1 << 20), (unsigned)std::min<int64_t>((a.MF + 3) / 4, 65535));
   const dim3 block(64, 4);
-  // F64E_RECON_GARNER=1 keeps exact products on the digit-by-digit kernels
-  // (A/B checks of the direct CRT form); read per call.
+  // F64E_RECON_FORM selects the exact-mode form for A/B checks (read per
+  // call): "f64" (default where M < 2^120), "crt" (direct CRT on the integer
+  // pipe), "garner" (digit by digit).  F64E_RECON_BESIDE chooses the form
+  // beside a resident GEMM chunk: "garner", or n = the FP64 form with its
+  // grid capped at n blocks per SM (the grid-stride loops cover the rest).
+  const char* fv = std::getenv("F64E_RECON_FORM");
   const char* gv = std::getenv("F64E_RECON_GARNER");
+  const char* bv = std::getenv("F64E_RECON_BESIDE");
+  bool want_garner = (gv && gv[0] == '1') || (fv && fv[0] == 'g');
+  const bool want_crt = fv && fv[0] == 'c';
+  if (beside_gemm && bv && bv[0] == 'g') want_garner = true;
+  if (beside_gemm && bv && bv[0] >= '1' && bv[0] <= '9' && sms > 0) {
+    const int64_t cap = (int64_t)std::atoi(bv) * sms;
+    grid.y = (unsigned)std::max<int64_t>(1, std::min<int64_t>(grid.y, cap / std::max<unsigned>(grid.x, 1u)));
+  }
+  if (a.exact && !want_garner && !want_crt) {
+    const Crt64Tables& C = crt64_tables(T);
+    if (C.ok) {
+      const char* mv = std::getenv("F64E_RECON_MINB");
+      const int minb = mv ? std::atoi(mv) : 4;
+      // four blocks per SM (64 registers) where that needs no spills (no or
+      // one correction plane), three otherwise
+#define F64E_RF64(MB)                                                                          \
+  switch (a.corr_mode) {                                                                       \
+    case 0: reconstruct_f64_kernel<0, MB><<<grid, block, 0, s>>>(a, C); break;                 \
+    case 1: reconstruct_f64_kernel<1, MB><<<grid, block, 0, s>>>(a, C); break;                 \
+    case 2: reconstruct_f64_kernel<2, (MB > 3 ? 3 : MB)><<<grid, block, 0, s>>>(a, C); break;  \
+    default: reconstruct_f64_kernel<3, (MB > 3 ? 3 : MB)><<<grid, block, 0, s>>>(a, C); break; \
+  }
+      if (minb == 2) {
+        F64E_RF64(2)
+      } else if (minb == 4) {
+        F64E_RF64(4)
+      } else {
+        F64E_RF64(3)
+      }
+#undef F64E_RF64
+      return;
+    }
+  }
   // The direct CRT kernel is the faster one alone (64 registers, four blocks
   // per SM); beside a resident GEMM chunk the Garner kernel (112 registers: one
   // block beside the GEMM CTA) takes less from the GEMM, and the product is
   // faster with it there (measured on row-chunked 8192^3 products).
-  if (a.exact && T.crt_ok && !beside_gemm && !(gv && gv[0] == '1')) {
+  if (a.exact && T.crt_ok && (want_crt || !beside_gemm) && !want_garner) {
     switch (a.corr_mode) {
       case 0: reconstruct_crt_kernel<0><<<grid, block, 0, s>>>(a, T); break;
       case 1: reconstruct_crt_kernel<1><<<grid, block, 0, s>>>(a, T); break;

@@ -1,9 +1,10 @@
-"""The two exact reconstruction forms must agree bit for bit: the direct CRT
-sum (modulus sets with M < 2^121; chosen where the reconstruction runs alone)
-and the digit-by-digit balanced Garner form (chosen beside GEMM chunks;
-F64E_RECON_GARNER=1 forces it).  Every correction layout (none, one fused
-plane, two planes, deep-K int64 sums), several modulus counts, ragged shapes,
-batches and non-finite inputs; the CPU oracle pins one of each."""
+"""The three exact reconstruction forms must agree bit for bit: the CRT sum on
+the FP64 pipe (modulus sets with M < 2^120, the default), the direct CRT sum
+on the integer pipe (F64E_RECON_FORM=crt) and the digit-by-digit balanced
+Garner form (F64E_RECON_FORM=garner; every modulus set).  Every correction
+layout (none, one fused plane, two planes, deep-K int64 sums), several modulus
+counts, ragged shapes, batches, non-finite inputs and results that are
+subnormal or overflow; the CPU oracle pins one of each."""
 import os
 
 import numpy as np
@@ -24,21 +25,32 @@ def emu():
     return fp64_emu
 
 
-def _both(fn):
-    """(Garner form, default form) of the same product."""
-    old = os.environ.get("F64E_RECON_GARNER")
+def _forms(fn):
+    """The same product under each reconstruction form: (garner, crt, default)."""
+    old = os.environ.get("F64E_RECON_FORM")
+    out = []
     try:
-        os.environ["F64E_RECON_GARNER"] = "1"
-        g = fn()
-        os.environ.pop("F64E_RECON_GARNER")
-        c = fn()
+        for form in ("garner", "crt", None):
+            if form is None:
+                os.environ.pop("F64E_RECON_FORM", None)
+            else:
+                os.environ["F64E_RECON_FORM"] = form
+            out.append(fn())
     finally:
         if old is None:
-            os.environ.pop("F64E_RECON_GARNER", None)
+            os.environ.pop("F64E_RECON_FORM", None)
         else:
-            os.environ["F64E_RECON_GARNER"] = old
+            os.environ["F64E_RECON_FORM"] = old
     torch.cuda.synchronize()
-    return g, c
+    return out
+
+
+def _both(fn):
+    """(Garner form, default form) of the same product; the direct CRT form
+    must give the same bits too."""
+    g, c, d = _forms(fn)
+    assert torch.equal(g.view(torch.int64), c.view(torch.int64))
+    return g, d
 
 
 CASES = [
@@ -93,3 +105,19 @@ def test_crt_form_non_finite(emu):
     assert torch.equal(g.isnan(), c.isnan())
     assert torch.equal(torch.nan_to_num(g, nan=0.0), torch.nan_to_num(c, nan=0.0))
     assert np.array_equal(g.cpu().numpy().view(np.uint64), c.cpu().numpy().view(np.uint64))
+
+
+def test_forms_subnormal_and_overflowing_results(emu):
+    # the FP64 form takes its exact side path when a result is not a normal
+    # double: every element of these products is subnormal, or overflows
+    g0 = torch.Generator(device="cuda").manual_seed(12)
+    A = torch.randn(200, 512, dtype=torch.float64, device="cuda", generator=g0) * 2.0 ** -530
+    Bt = torch.randn(512, 150, dtype=torch.float64, device="cuda", generator=g0) * 2.0 ** -530
+    g, d = _both(lambda: emu.mm_nt(A, Bt))
+    assert (d.abs() < 2.0 ** -1022).float().mean() > 0.9
+    assert torch.equal(g.view(torch.int64), d.view(torch.int64))
+    A = A * 2.0 ** 525 * 2.0 ** 525
+    Bt = Bt * 2.0 ** 520 * 2.0 ** 520
+    g, d = _both(lambda: emu.mm_nt(A, Bt))
+    assert torch.isinf(d).float().mean() > 0.5
+    assert torch.equal(g.view(torch.int64), d.view(torch.int64))

@@ -28,7 +28,7 @@ CXX = "/usr/bin/g++"
 
 CUDA_SOURCES = ["f64e_api.cu", "f64e_sizing.cu", "f64e_extract.cu", "f64e_gemm.cu", "f64e_gemm_check.cu",
                 "f64e_recon.cu", "f64e_deepk.cu", "f64e_noalloc.cu"]
-HEADERS = ["f64e_device.cuh", "f64e_params.h", "f64e_kernels.h"]
+HEADERS = ["f64e_device.cuh", "f64e_params.h", "f64e_kernels.h", "f64e_crt64.cuh"]
 NVCC_FLAGS = ["-std=c++17", "-O3", "-lineinfo", "-gencode", "arch=compute_100a,code=sm_100a",
               "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden", "-ccbin", CXX,
               f"-I{INCLUDE}", f"-I{CSRC}"]

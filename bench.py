@@ -856,6 +856,65 @@ def run_int8_peak(args):
                                     "gpu": torch.cuda.get_device_name(dev)}}), flush=True)
 
 
+# ------------------------------------------------------------ PCIe probe --
+def run_pcie_probe(args):
+    """Host <-> device copy rates of every rank at once (one process per GPU,
+    as the end-to-end runs): pinned 1 GiB buffers, one cudaMemcpyAsync per
+    copy (torch's copy_), host-to-device alone, device-to-host alone, and both
+    directions at once on two streams; CUDA events, the slowest rank's time.
+    Run twice: with the buffers allocated after binding the process to its
+    GPU's NUMA-local cores (fp64_emu.host.bind_to_gpu_cpus), and without."""
+    rank, world = (dist.get_rank(), dist.get_world_size()) if dist.is_initialized() else (0, 1)
+    dev = torch.device("cuda", torch.cuda.current_device())
+    nbytes = args.probe_mib << 20
+    res = {}
+    for placement in ("default", "gpu_local"):
+        cpus = None
+        if placement == "gpu_local":
+            from fp64_emu.host import bind_to_gpu_cpus
+            cpus = bind_to_gpu_cpus(dev)
+        h_in = torch.empty(nbytes, dtype=torch.uint8).pin_memory()
+        h_out = torch.empty(nbytes, dtype=torch.uint8).pin_memory()
+        h_in.fill_(1)
+        h_out.fill_(2)
+        d_in = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+        d_out = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+        s1, s2 = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+        out = {}
+        for mode in ("h2d", "d2h", "both"):
+            best = float("inf")
+            for it in range(4):
+                barrier()
+                torch.cuda.synchronize()
+                e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+                e0.record(s1)
+                s2.wait_event(e0)
+                if mode in ("h2d", "both"):
+                    with torch.cuda.stream(s1):
+                        d_in.copy_(h_in, non_blocking=True)
+                if mode in ("d2h", "both"):
+                    with torch.cuda.stream(s2):
+                        h_out.copy_(d_out, non_blocking=True)
+                e1.record(s1)
+                e2.record(s2)
+                torch.cuda.synchronize()
+                ms = max(e0.elapsed_time(e1), e0.elapsed_time(e2))
+                if it > 0:
+                    best = min(best, max_over_ranks(ms))
+                else:
+                    max_over_ranks(ms)
+            moved = nbytes * (2 if mode == "both" else 1)
+            out[mode] = {"per_rank_gbs": round(moved / (best * 1e-3) / 1e9, 1),
+                         "aggregate_gbs": round(world * moved / (best * 1e-3) / 1e9, 1), "ms": round(best, 3)}
+        out["cpus"] = (f"{len(cpus)} cores {min(cpus)}-{max(cpus)}" if cpus else "unchanged")
+        res[placement] = out
+        del h_in, h_out, d_in, d_out
+    if rank == 0:
+        print(json.dumps({"pcie_probe": res, "n_gpus": world, "bytes_per_copy": nbytes,
+                          "note": "slowest rank's time of each copy pattern, best of 3 after one warm-up"}),
+              flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -873,6 +932,9 @@ def main():
                     help="N > 1: skip the unpartitioned recomputation that checks every rank's block")
     ap.add_argument("--int8-peak", action="store_true",
                     help="measure the dense INT8 GEMM peak (cuBLAS through torch._int_mm) and exit")
+    ap.add_argument("--pcie-probe", action="store_true",
+                    help="measure every rank's pinned host <-> device copy rates at once and exit")
+    ap.add_argument("--probe-mib", type=int, default=1024)
     ap.add_argument("--peak-n", type=int, default=8192)
     ap.add_argument("--peak-seconds", type=float, default=4.0)
     args = ap.parse_args()
@@ -887,6 +949,8 @@ def main():
     try:
         if args.int8_peak:
             run_int8_peak(args)
+        elif args.pcie_probe:
+            run_pcie_probe(args)
         elif args.impl == "reference":
             run_reference(args)
         else:

@@ -189,6 +189,18 @@ F64E_HD double crt64_finish(const Crt64Tables& T, double a0, double a1, double a
   return crt64_scale2(big ? big_r : small_r, big ? sh + 40 : sh);
 }
 
+// Host: the device kernel's scaling of built tables.  The kernel feeds u_t
+// as the subnormal u_t 2^-1042 (its byte in the high word of a double with a
+// zero exponent field: no conversion, no subtraction), so the limbs are
+// scaled by 2^978 (below 2^1018) and each product is u_t e_{t,l} 2^-64; the
+// starting sums take the same 2^-64, and the kernel multiplies the sums by
+// 2^64 (exact) before crt64_finish.
+inline void crt64_device_scale(Crt64Tables* T) {
+  for (int t = 0; t < T->P; t++)
+    for (int l = 0; l < 3; l++) T->e[t][l] = std::ldexp(T->e[t][l], 32 + 978);
+  for (int l = 0; l < 3; l++) T->z[l] = std::ldexp(T->z[l], -64);
+}
+
 // Host: the tables of a modulus list; false (ok = 0) when M >= 2^120 or the
 // moduli are not pairwise coprime.
 inline bool crt64_build(const int32_t* primes, int P, float log2M, Crt64Tables* T) {

@@ -443,17 +443,23 @@ __global__ void __launch_bounds__(256, 4) reconstruct_crt_kernel(const ReconArgs
 
 
 // FP64-pipe CRT form (exact mode, M < 2^120; f64e_crt64.cuh): the limb sums
-// sum_t u_t e_{t,l} as fused multiply-adds of exact doubles.  u_t * 2^32 is
-// built from the stored byte without a conversion: one byte_perm places the
-// byte, top bit flipped (u_t = r_t + 128), under the exponent of 2^52, and
-// subtracting 2^52 leaves u_t * 2^32 exactly.  Block (64, 4): x spans 64
-// four-column chunks of a row, y four rows; each thread reads one 32-bit word
-// (four columns) per residue plane.
-template <int CM, int MINB>
+// sum_t u_t e_{t,l} as fused multiply-adds of exact doubles.  u_t enters
+// without a conversion: one byte_perm places the byte, top bit flipped
+// (u_t = r_t + 128), in the high word of a double whose exponent field is 0,
+// i.e. the subnormal u_t * 2^-1042 (FP64 arithmetic keeps subnormals exact
+// and at full rate); the table limbs are scaled by 2^978 (crt64_device_tables),
+// so every product is u_t e_{t,l} 2^-64 exactly and the sums are the integer
+// limb sums times 2^-64.  Block (64, 4): x spans 64 four-column chunks of a
+// row, y four rows; each thread reads one 32-bit word (four columns) per
+// residue plane.  NP > 0 fixes the modulus count at compile time (the default
+// plans' 13, 14 and 15), so the modulus loop has no branches and its loads
+// and multiply-adds interleave freely; NP = 0 takes T.P.
+template <int CM, int MINB, int NP>
 __global__ void __launch_bounds__(256, MINB) reconstruct_f64_kernel(const ReconArgs a, const Crt64Tables T) {
+  constexpr int PMAX = NP > 0 ? NP : kMaxP;
   const Gain gn = pick_gain(a.maxlg[0], a.maxlg[1], T.log2M, a.bits);
   const double csc = crt64_pow2(gn.bits_eff - 15 - 40);
-  const int P = T.P;
+  const int P = NP > 0 ? NP : T.P;
   const int64_t nq = (a.N + 3) >> 2;
   const int64_t plane = a.MF * a.ldn;
   const bool vec_out = ((a.ldc & 3) == 0) && ((reinterpret_cast<uintptr_t>(a.C) & 15) == 0);
@@ -463,12 +469,11 @@ __global__ void __launch_bounds__(256, MINB) reconstruct_f64_kernel(const ReconA
     for (int64_t jq = (int64_t)blockIdx.x * 64 + threadIdx.x; jq < nq; jq += (int64_t)gridDim.x * 64) {
       const int64_t j0 = jq << 2;
       const int64_t off = i * a.ldn + j0;
-      uint32_t rw[kMaxP];
+      const int8_t* rp = a.res + off;
+      uint32_t rw[PMAX];
 #pragma unroll
-      for (int t = 0; t < kMaxP; t++)
-        rw[t] = (t < P) ? __ldg(reinterpret_cast<const unsigned int*>(a.res + t * plane + off)) : 0u;
-#pragma unroll
-      for (int t = 0; t < kMaxP; t++) rw[t] ^= 0x80808080u;   // u_t = r_t + 128 per byte
+      for (int t = 0; t < PMAX; t++)
+        rw[t] = (NP > 0 || t < P) ? __ldg(reinterpret_cast<const unsigned int*>(rp + t * plane)) ^ 0x80808080u : 0u;
       int64_t cr[4];
       load_corr<CM>(a, off, plane, cr);
       double outv[4];
@@ -477,9 +482,9 @@ __global__ void __launch_bounds__(256, MINB) reconstruct_f64_kernel(const ReconA
       for (int e = 0; e < 4; e++) {
         double a0 = T.z[0], a1 = T.z[1], a2 = T.z[2];
 #pragma unroll
-        for (int t = 0; t < kMaxP; t++) {
-          if (t >= P) break;
-          const double du = __hiloint2double((int)__byte_perm(rw[t], 0x43300000u, 0x7650u | (uint32_t)e), 0) - 0x1p52;
+        for (int t = 0; t < PMAX; t++) {
+          if (NP == 0 && t >= P) break;
+          const double du = __hiloint2double((int)__byte_perm(rw[t], 0u, 0x4440u | (uint32_t)e), 0);
           a0 = fma(du, T.e[t][0], a0);
           a1 = fma(du, T.e[t][1], a1);
           a2 = fma(du, T.e[t][2], a2);
@@ -487,7 +492,8 @@ __global__ void __launch_bounds__(256, MINB) reconstruct_f64_kernel(const ReconA
         const int64_t j = j0 + e;
         const int sh = -sa - (j < a.N ? (int)sB[j] + gn.g : 0);
         double r;
-        if (!crt64_finish_fast(T, a0, a1, a2, (double)cr[e], csc, sh, &r)) slow |= 1u << e;
+        if (!crt64_finish_fast(T, a0 * 0x1p64, a1 * 0x1p64, a2 * 0x1p64, (double)cr[e], csc, sh, &r))
+          slow |= 1u << e;
         outv[e] = r;
       }
       double* crow = a.C + i * a.ldc;
@@ -510,22 +516,25 @@ __global__ void __launch_bounds__(256, MINB) reconstruct_f64_kernel(const ReconA
           double a0 = T.z[0], a1 = T.z[1], a2 = T.z[2];
 #pragma unroll 1
           for (int t = 0; t < P; t++) {
-            const double du = (double)((uint32_t)(uint8_t)a.res[t * plane + off + e] ^ 0x80u) * 0x1p32;
+            const double du = (double)((uint32_t)(uint8_t)rp[t * plane + e] ^ 0x80u) * 0x1p-1042;
             a0 = fma(du, T.e[t][0], a0);
             a1 = fma(du, T.e[t][1], a1);
             a2 = fma(du, T.e[t][2], a2);
           }
           const int sh = -sa - ((int)sB[j0 + e] + gn.g);
           const int64_t ce = e == 0 ? cr[0] : (e == 1 ? cr[1] : (e == 2 ? cr[2] : cr[3]));
-          crow[j0 + e] = crt64_finish(T, a0, a1, a2, (double)ce, csc, sh);
+          crow[j0 + e] = crt64_finish(T, a0 * 0x1p64, a1 * 0x1p64, a2 * 0x1p64, (double)ce, csc, sh);
         }
       }
     }
   }
 }
 
-// Tables of the FP64 CRT form for a modulus set, built once per set.
-const Crt64Tables& crt64_tables(const ModTables& T) {
+// Tables of the FP64 CRT form for a modulus set, built once per set, in the
+// device kernel's scaling: limbs e_{t,l} times 2^978 (u_t enters as the
+// subnormal u_t 2^-1042, so each product is u_t e_{t,l} 2^-64) and the
+// starting sums -z_l times 2^-64.
+const Crt64Tables& crt64_device_tables(const ModTables& T) {
   static std::mutex mtx;
   static std::map<std::vector<int32_t>, Crt64Tables> cache;
   std::vector<int32_t> key(T.p, T.p + T.P);
@@ -533,12 +542,11 @@ const Crt64Tables& crt64_tables(const ModTables& T) {
   auto it = cache.find(key);
   if (it == cache.end()) {
     Crt64Tables C;
-    crt64_build(key.data(), T.P, T.log2M, &C);
+    if (crt64_build(key.data(), T.P, T.log2M, &C)) crt64_device_scale(&C);
     it = cache.emplace(key, C).first;
   }
   return it->second;
 }
-
 
 void launch_reconstruct(const ReconArgs& a, const ModTables& T, cudaStream_t s, bool beside_gemm, int sms) {
   if (a.MF <= 0 || a.N <= 0) return;
@@ -548,40 +556,44 @@ void launch_reconstruct(const ReconArgs& a, const ModTables& T, cudaStream_t s, 
   // F64E_RECON_FORM selects the exact-mode form for A/B checks (read per
   // call): "f64" (default where M < 2^120), "crt" (direct CRT on the integer
   // pipe), "garner" (digit by digit).  F64E_RECON_BESIDE chooses the form
-  // beside a resident GEMM chunk: "garner", or n = the FP64 form with its
-  // grid capped at n blocks per SM (the grid-stride loops cover the rest).
+  // beside a resident GEMM chunk: "garner" (default), "f64", or n = the FP64
+  // form with its grid capped at n blocks per SM (the grid-stride loops cover
+  // the rest).
   const char* fv = std::getenv("F64E_RECON_FORM");
   const char* gv = std::getenv("F64E_RECON_GARNER");
   const char* bv = std::getenv("F64E_RECON_BESIDE");
   bool want_garner = (gv && gv[0] == '1') || (fv && fv[0] == 'g');
   const bool want_crt = fv && fv[0] == 'c';
-  if (beside_gemm && bv && bv[0] == 'g') want_garner = true;
+  // Beside a resident GEMM chunk the digit-by-digit form is the default:
+  // there the FP64 form's blocks crowd out the extraction of the next chunk
+  // (measured on row-chunked 8192^3 products: 157 against 154 TFLOP/s).
+  if (beside_gemm && !(bv && (bv[0] == 'f' || (bv[0] >= '1' && bv[0] <= '9')))) want_garner = true;
   if (beside_gemm && bv && bv[0] >= '1' && bv[0] <= '9' && sms > 0) {
     const int64_t cap = (int64_t)std::atoi(bv) * sms;
     grid.y = (unsigned)std::max<int64_t>(1, std::min<int64_t>(grid.y, cap / std::max<unsigned>(grid.x, 1u)));
   }
   if (a.exact && !want_garner && !want_crt) {
-    const Crt64Tables& C = crt64_tables(T);
+    const Crt64Tables& C = crt64_device_tables(T);
     if (C.ok) {
-      const char* mv = std::getenv("F64E_RECON_MINB");
-      const int minb = mv ? std::atoi(mv) : 4;
-      // four blocks per SM (64 registers) where that needs no spills (no or
-      // one correction plane), three otherwise
-#define F64E_RF64(MB)                                                                          \
-  switch (a.corr_mode) {                                                                       \
-    case 0: reconstruct_f64_kernel<0, MB><<<grid, block, 0, s>>>(a, C); break;                 \
-    case 1: reconstruct_f64_kernel<1, MB><<<grid, block, 0, s>>>(a, C); break;                 \
-    case 2: reconstruct_f64_kernel<2, (MB > 3 ? 3 : MB)><<<grid, block, 0, s>>>(a, C); break;  \
-    default: reconstruct_f64_kernel<3, (MB > 3 ? 3 : MB)><<<grid, block, 0, s>>>(a, C); break; \
-  }
-      if (minb == 2) {
-        F64E_RF64(2)
-      } else if (minb == 4) {
-        F64E_RF64(4)
-      } else {
-        F64E_RF64(3)
+      const int np = (T.P == 13 || T.P == 14 || T.P == 15) ? T.P : 0;
+#define F64E_RF64_NP(CMV, MB, NPV) reconstruct_f64_kernel<CMV, MB, NPV><<<grid, block, 0, s>>>(a, C)
+#define F64E_RF64_CM(CMV, MB)                  \
+  do {                                         \
+    if (np == 14) F64E_RF64_NP(CMV, MB, 14);      \
+    else if (np == 15) F64E_RF64_NP(CMV, MB, 15); \
+    else if (np == 13) F64E_RF64_NP(CMV, MB, 13); \
+    else F64E_RF64_NP(CMV, MB, 0);             \
+  } while (0)
+      // three blocks per SM (80 registers); the int64 deep-K correction
+      // layout, rare, takes the generic modulus count only
+      switch (a.corr_mode) {
+        case 0: F64E_RF64_CM(0, 3); break;
+        case 1: F64E_RF64_CM(1, 3); break;
+        case 2: F64E_RF64_CM(2, 3); break;
+        default: F64E_RF64_NP(3, 3, 0); break;
       }
-#undef F64E_RF64
+#undef F64E_RF64_CM
+#undef F64E_RF64_NP
       return;
     }
   }

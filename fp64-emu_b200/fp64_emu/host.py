@@ -16,10 +16,45 @@ of the three.  The single-call form of the same idea is fp64_emu.mm_nt_host
 
 Results are bit-identical to the device-resident call of the same kind.
 """
+import os
+
 import torch
 
 from . import _defaults, _tables
 from ._ops import ops
+
+
+def gpu_local_cpus(device=None):
+    """The CPU cores NVML reports as local to `device` (its NUMA node's
+    cores), or None when NVML cannot tell.  Read only: no GPU setting is
+    touched."""
+    try:
+        import pynvml
+        idx = torch.cuda.current_device() if device is None else torch.device(device).index
+        uuid = str(torch.cuda.get_device_properties(idx).uuid)
+        pynvml.nvmlInit()
+        try:
+            h = pynvml.nvmlDeviceGetHandleByUUID(uuid if uuid.startswith("GPU-") else "GPU-" + uuid)
+            words = (os.cpu_count() + 63) // 64
+            mask = pynvml.nvmlDeviceGetCpuAffinity(h, words)
+        finally:
+            pynvml.nvmlShutdown()
+        cpus = [64 * w + b for w, m in enumerate(mask) for b in range(64) if (int(m) >> b) & 1]
+        cpus = [c for c in cpus if c < os.cpu_count()]
+        return cpus or None
+    except Exception:  # noqa: BLE001  (no NVML, no permission, unknown device)
+        return None
+
+
+def bind_to_gpu_cpus(device=None):
+    """Restrict this process to the cores local to `device`, so page-locked
+    buffers allocated afterwards are first touched on the GPU's NUMA node and
+    host-device copies do not cross the socket link.  Returns the cores, or
+    None (affinity unchanged) when they are unknown."""
+    cpus = gpu_local_cpus(device)
+    if cpus:
+        os.sched_setaffinity(0, cpus)
+    return cpus
 
 _KINDS = {"mm": False, "mm_nt": True, "bmm": False, "bmm_nt": True}
 

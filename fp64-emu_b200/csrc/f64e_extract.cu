@@ -200,10 +200,14 @@ __device__ __forceinline__ void store_corr(const Split (&S)[8], bool corr, const
 // registers for the residue loop (64 registers in extract_cols: four blocks
 // per SM).  The row kernel keeps them last: beside a resident GEMM chunk its
 // measured products were faster that way.
-template <bool CORR_FIRST>
+// NP > 0 fixes the modulus count at compile time (the default plans' 14 and
+// 15): the plane loop then has no branches and the planes' arithmetic and
+// stores interleave; NP = 0 takes T.P.
+template <bool CORR_FIRST, int NP>
 __device__ __forceinline__ void extract8(const double (&x)[8], int s, bool fast, double p2s, double p2h, int be,
                                          bool corr, const ExtractArgs& a, const ModTables& T, int8_t* dst) {
-  const int P = T.P;
+  constexpr int PMAX = NP > 0 ? NP : kMaxP;
+  const int P = NP > 0 ? NP : T.P;
   const int64_t pstride = a.pstride;
   Split S[8];
   const uint64_t bias = 1ULL << be;
@@ -218,8 +222,8 @@ __device__ __forceinline__ void extract8(const double (&x)[8], int s, bool fast,
   // non-finite maximum (u >= 2^56).
   if ((top >> 24) == 0) {
 #pragma unroll
-    for (int t = 0; t < kMaxP; t++) {
-      if (t >= P) break;
+    for (int t = 0; t < PMAX; t++) {
+      if (NP == 0 && t >= P) break;
       uint32_t w[2];
       residue_words<8>(S, T, t, be, w);
       *reinterpret_cast<uint2*>(dst + t * pstride) = make_uint2(w[0], w[1]);
@@ -239,7 +243,7 @@ __device__ __forceinline__ void extract8(const double (&x)[8], int s, bool fast,
 // 8 consecutive columns of one row; a warp covers 256 columns (2 KB read,
 // 256 B written per plane, both contiguous).  (bx, by) of a (gdx, gdy) grid,
 // with grid-stride loops over the K chunks and the rows.
-template <bool VEC>
+template <bool VEC, int NP>
 __device__ __forceinline__ void extract_rows_body(const ExtractArgs& a, const ModTables& T, int bx, int by, int gdx,
                                                   int gdy, int tx, int ty) {
   const Gain gn = pick_gain(a.maxlg[0], a.maxlg[1], T.log2M, a.bits);
@@ -266,7 +270,7 @@ __device__ __forceinline__ void extract_rows_body(const ExtractArgs& a, const Mo
 #pragma unroll
         for (int u = 0; u < 8; u++) x[u] = (k0 + u < a.K) ? __ldg(xr + k0 + u) : 0.0;
       }
-      extract8<false>(x, s, row_fast, p2s, p2h, be, corr, a, T, a.planes + r * a.Kp + k0);
+      extract8<false, NP>(x, s, row_fast, p2s, p2h, be, corr, a, T, a.planes + r * a.Kp + k0);
     }
   }
 }
@@ -276,10 +280,10 @@ __device__ __forceinline__ void extract_rows_body(const ExtractArgs& a, const Mo
 // (79 registers, no spills): the kernel waits on its loads, and the third
 // block hides more of that than the register cap costs (measured: 8192^2
 // operands extract in 0.92-0.95 ms against 1.03-1.07 ms at two blocks).
-template <bool VEC, bool PAIR>
+template <bool VEC, bool PAIR, int NP>
 __global__ void __launch_bounds__(256, 3) extract_rows_kernel(const ExtractPair ap, const ModTables T) {
-  extract_rows_body<VEC>(ap.a[PAIR ? blockIdx.z : 0], T, (int)blockIdx.x, (int)blockIdx.y, (int)gridDim.x,
-                         (int)gridDim.y, (int)threadIdx.x, (int)threadIdx.y);
+  extract_rows_body<VEC, NP>(ap.a[PAIR ? blockIdx.z : 0], T, (int)blockIdx.x, (int)blockIdx.y, (int)gridDim.x,
+                             (int)gridDim.y, (int)threadIdx.x, (int)threadIdx.y);
 }
 
 // [batch, K, N] operand: a block takes a 64 (k) x 32 (n) tile.  Warp w reads
@@ -295,6 +299,7 @@ constexpr int kColTileK = 64, kColTileN = 32, kColPitch = 66;
 // Tile (bx: n tiles, by: K tiles, bz: batch member) of a [batch, K, N]
 // operand, by a 256-thread block with xs[kColTileN * kColPitch] of shared
 // memory.  One barrier, reached by every thread of the block.
+template <int NP>
 __device__ __forceinline__ void extract_cols_body(const ExtractArgs& a, const ModTables& T, int bx, int by, int bz,
                                                   double* xs) {
   const int64_t b = bz;
@@ -329,13 +334,14 @@ __device__ __forceinline__ void extract_cols_body(const ExtractArgs& a, const Mo
   const int be = gn.bits_eff;
   const int s = (int)a.sft[b * a.N + n] + gn.g;
   const bool fast = (s >= -960) && (s <= 960);
-  extract8<true>(x, s, fast, pow2d(fast ? s : 0), pow2d(7 - be), be, a.use_corr != 0, a, T,
+  extract8<true, NP>(x, s, fast, pow2d(fast ? s : 0), pow2d(7 - be), be, a.use_corr != 0, a, T,
                  a.planes + (b * a.N + n) * a.Kp + kk);
 }
 
+template <int NP>
 __global__ void __launch_bounds__(256, 2) extract_cols_kernel(const ExtractArgs a, const ModTables T) {
   __shared__ __align__(16) double xs[kColTileN * kColPitch];
-  extract_cols_body(a, T, (int)blockIdx.x, (int)blockIdx.y, (int)blockIdx.z, xs);
+  extract_cols_body<NP>(a, T, (int)blockIdx.x, (int)blockIdx.y, (int)blockIdx.z, xs);
 }
 
 // A [rows, K] operand and a [batch, K, N] operand in one launch (small nt
@@ -348,11 +354,12 @@ __global__ void __launch_bounds__(256, 2) extract_nt_pair_kernel(const ExtractAr
   __shared__ __align__(16) double xs[kColTileN * kColPitch];
   const int i = (int)blockIdx.x;
   if (i < na) {
-    extract_rows_body<VEC>(ra, T, i % gxa, i / gxa, gxa, na / gxa, (int)(threadIdx.x & 31), (int)(threadIdx.x >> 5));
+    extract_rows_body<VEC, 0>(ra, T, i % gxa, i / gxa, gxa, na / gxa, (int)(threadIdx.x & 31),
+                              (int)(threadIdx.x >> 5));
   } else {
     const int j = i - na, per = gxb * gyb;
     const int bz = j / per, r = j - bz * per;
-    extract_cols_body(cb, T, r % gxb, r / gxb, bz, xs);
+    extract_cols_body<0>(cb, T, r % gxb, r / gxb, bz, xs);
   }
 }
 
@@ -370,8 +377,14 @@ void launch_extract_rows(const ExtractArgs& a, const ModTables& T, cudaStream_t 
   ExtractPair ap;
   ap.a[0] = a;
   ap.a[1] = a;
-  if (rows_vec(a)) extract_rows_kernel<true, false><<<dim3(gx, gy), dim3(32, 8), 0, s>>>(ap, T);
-  else extract_rows_kernel<false, false><<<dim3(gx, gy), dim3(32, 8), 0, s>>>(ap, T);
+  const dim3 grid(gx, gy), block(32, 8);
+  if (rows_vec(a)) {
+    if (T.P == 14) extract_rows_kernel<true, false, 14><<<grid, block, 0, s>>>(ap, T);
+    else if (T.P == 15) extract_rows_kernel<true, false, 15><<<grid, block, 0, s>>>(ap, T);
+    else extract_rows_kernel<true, false, 0><<<grid, block, 0, s>>>(ap, T);
+  } else {
+    extract_rows_kernel<false, false, 0><<<grid, block, 0, s>>>(ap, T);
+  }
 }
 
 void launch_extract_rows_pair(const ExtractArgs& a0, const ExtractArgs& a1, const ModTables& T, cudaStream_t s) {
@@ -386,8 +399,8 @@ void launch_extract_rows_pair(const ExtractArgs& a0, const ExtractArgs& a1, cons
   ExtractPair ap;
   ap.a[0] = a0;
   ap.a[1] = a1;
-  if (rows_vec(a0) && rows_vec(a1)) extract_rows_kernel<true, true><<<dim3(gx, gy, 2), dim3(32, 8), 0, s>>>(ap, T);
-  else extract_rows_kernel<false, true><<<dim3(gx, gy, 2), dim3(32, 8), 0, s>>>(ap, T);
+  if (rows_vec(a0) && rows_vec(a1)) extract_rows_kernel<true, true, 0><<<dim3(gx, gy, 2), dim3(32, 8), 0, s>>>(ap, T);
+  else extract_rows_kernel<false, true, 0><<<dim3(gx, gy, 2), dim3(32, 8), 0, s>>>(ap, T);
 }
 
 void launch_extract_nt_pair(const ExtractArgs& ra, const ExtractArgs& cb, const ModTables& T, cudaStream_t s) {
@@ -417,7 +430,9 @@ void launch_extract_cols(const ExtractArgs& a, const ModTables& T, cudaStream_t 
   if (a.N <= 0 || a.Kp <= 0 || a.batch <= 0) return;
   const dim3 grid((unsigned)((a.N + kColTileN - 1) / kColTileN), (unsigned)((a.Kp + kColTileK - 1) / kColTileK),
                   (unsigned)a.batch);
-  extract_cols_kernel<<<grid, 256, 0, s>>>(a, T);
+  if (T.P == 14) extract_cols_kernel<14><<<grid, 256, 0, s>>>(a, T);
+  else if (T.P == 15) extract_cols_kernel<15><<<grid, 256, 0, s>>>(a, T);
+  else extract_cols_kernel<0><<<grid, 256, 0, s>>>(a, T);
 }
 
 }  // namespace f64e

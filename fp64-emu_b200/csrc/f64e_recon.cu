@@ -245,11 +245,14 @@ __host__ __device__ constexpr uint32_t insert_sel(int k) {
 
 // Fast form (every modulus > 128): digits kept offset, d' = d + h in [0, p),
 // exact quotients, no correction steps (constants: ModTables fast forms).
-template <int CM, bool EXACT>
+// NP > 0 fixes the modulus count at compile time (the default plans' 14 and
+// 15): no branch inside the digit loop; NP = 0 takes T.P.
+template <int CM, bool EXACT, int NP>
 __global__ void __launch_bounds__(256, 2) reconstruct_fast_kernel(const ReconArgs a, const ModTables T) {
+  constexpr int PMAX = NP > 0 ? NP : kMaxP;
   const Gain gn = pick_gain(a.maxlg[0], a.maxlg[1], T.log2M, a.bits);
   const int cshift = gn.bits_eff - 15;
-  const int P = T.P;
+  const int P = NP > 0 ? NP : T.P;
   const int ng = (P + 6) / 7;
   const int64_t nq = (a.N + 3) >> 2;
   const int64_t plane = a.MF * a.ldn;
@@ -260,10 +263,10 @@ __global__ void __launch_bounds__(256, 2) reconstruct_fast_kernel(const ReconArg
     for (int64_t jq = (int64_t)blockIdx.x * 64 + threadIdx.x; jq < nq; jq += (int64_t)gridDim.x * 64) {
       const int64_t j0 = jq << 2;
       const int64_t off = i * a.ldn + j0;
-      uint32_t rw[kMaxP];
+      uint32_t rw[PMAX];
 #pragma unroll
-      for (int t = 0; t < kMaxP; t++)
-        rw[t] = (t < P) ? __ldg(reinterpret_cast<const unsigned int*>(a.res + t * plane + off)) : 0u;
+      for (int t = 0; t < PMAX; t++)
+        rw[t] = (NP > 0 || t < P) ? __ldg(reinterpret_cast<const unsigned int*>(a.res + t * plane + off)) : 0u;
       int64_t cr[4];
       load_corr<CM>(a, off, plane, cr);
       uint32_t dp[4][kGroups];
@@ -283,8 +286,8 @@ __global__ void __launch_bounds__(256, 2) reconstruct_fast_kernel(const ReconArg
         }
       }
 #pragma unroll
-      for (int t = 0; t < kMaxP; t++) {
-        if (t >= P) break;
+      for (int t = 0; t < PMAX; t++) {
+        if (NP == 0 && t >= P) break;
         const uint32_t p = T.p[t], mr = T.mrec[t], kr = T.krec[t];
         const int mi = T.minv[t];
 #pragma unroll
@@ -611,19 +614,29 @@ void launch_reconstruct(const ReconArgs& a, const ModTables& T, cudaStream_t s, 
     return;
   }
   if (T.fast_recon) {
+    // the default plans' common layouts (exact, one correction plane, 14 or
+    // 15 moduli) with the modulus count fixed at compile time
+    if (a.exact && a.corr_mode == 1 && T.P == 14) {
+      reconstruct_fast_kernel<1, true, 14><<<grid, block, 0, s>>>(a, T);
+      return;
+    }
+    if (a.exact && a.corr_mode == 1 && T.P == 15) {
+      reconstruct_fast_kernel<1, true, 15><<<grid, block, 0, s>>>(a, T);
+      return;
+    }
     if (a.exact) {
       switch (a.corr_mode) {
-        case 0: reconstruct_fast_kernel<0, true><<<grid, block, 0, s>>>(a, T); break;
-        case 1: reconstruct_fast_kernel<1, true><<<grid, block, 0, s>>>(a, T); break;
-        case 2: reconstruct_fast_kernel<2, true><<<grid, block, 0, s>>>(a, T); break;
-        default: reconstruct_fast_kernel<3, true><<<grid, block, 0, s>>>(a, T); break;
+        case 0: reconstruct_fast_kernel<0, true, 0><<<grid, block, 0, s>>>(a, T); break;
+        case 1: reconstruct_fast_kernel<1, true, 0><<<grid, block, 0, s>>>(a, T); break;
+        case 2: reconstruct_fast_kernel<2, true, 0><<<grid, block, 0, s>>>(a, T); break;
+        default: reconstruct_fast_kernel<3, true, 0><<<grid, block, 0, s>>>(a, T); break;
       }
     } else {
       switch (a.corr_mode) {
-        case 0: reconstruct_fast_kernel<0, false><<<grid, block, 0, s>>>(a, T); break;
-        case 1: reconstruct_fast_kernel<1, false><<<grid, block, 0, s>>>(a, T); break;
-        case 2: reconstruct_fast_kernel<2, false><<<grid, block, 0, s>>>(a, T); break;
-        default: reconstruct_fast_kernel<3, false><<<grid, block, 0, s>>>(a, T); break;
+        case 0: reconstruct_fast_kernel<0, false, 0><<<grid, block, 0, s>>>(a, T); break;
+        case 1: reconstruct_fast_kernel<1, false, 0><<<grid, block, 0, s>>>(a, T); break;
+        case 2: reconstruct_fast_kernel<2, false, 0><<<grid, block, 0, s>>>(a, T); break;
+        default: reconstruct_fast_kernel<3, false, 0><<<grid, block, 0, s>>>(a, T); break;
       }
     }
     return;

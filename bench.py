@@ -429,13 +429,16 @@ def run_ours(args):
         part = f"2-D C blocks {pr}x{pc}"
     A_host_full = A.cpu() if (rank == 0 and world == 1 and not args.no_cpu) else None
     B_host_full = B.cpu() if (rank == 0 and world == 1 and not args.no_cpu) else None
-    shs = shares = None
+    shs = shares = host_cpus = None
     if world > 1 and batch == 1:
         # e2e at N > 1: every rank copies in a disjoint share of its blocks and
         # the blocks are completed over NVLink (fp64_emu.dist.ShardedHostStream)
         from fp64_emu.dist import ShardedHostStream
+        from fp64_emu.host import gpu_local_allocation
         shs = ShardedHostStream(kind, M, N, K, nprimes=nprimes, corr=corr)
-        shares = shs.host_shares(A.cpu(), B.cpu())
+        with gpu_local_allocation(dev) as loc:   # page-locked shares on the GPU's NUMA node
+            shares = shs.host_shares(A.cpu(), B.cpu())
+            host_cpus = loc.cpus
     del A, B
     torch.cuda.empty_cache()
 
@@ -469,9 +472,12 @@ def run_ours(args):
     # e2e through the public API with host buffers.
     import fp64_emu
     if shs is None:
-        A_pin = A_l.cpu().pin_memory()
-        B_pin = B_l.cpu().pin_memory()
-        out_pin = torch.empty(step.out.shape, dtype=torch.float64).pin_memory()
+        from fp64_emu.host import gpu_local_allocation
+        with gpu_local_allocation(dev) as loc:   # page-locked buffers on the GPU's NUMA node
+            A_pin = A_l.cpu().pin_memory()
+            B_pin = B_l.cpu().pin_memory()
+            out_pin = torch.empty(step.out.shape, dtype=torch.float64).pin_memory()
+            host_cpus = loc.cpus
         A_d = torch.empty_like(A_l)
         B_d = torch.empty_like(B_l)
 
@@ -559,6 +565,8 @@ def run_ours(args):
         "compute": "s8 x s8 -> s32 tcgen05 residue GEMMs, exact int128 recombine",
         "e2e": {"value": round(work / (e2e_ms * 1e-3) / 1e12, 3), "unit": UNIT, "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h,
+                "host_buffers": (f"page-locked on the GPU's NUMA node (allocated on {len(host_cpus)} local cores)"
+                                 if host_cpus else "page-locked, default placement"),
                 "api": ("fp64_emu.HostStream (operand copies, product and result copy of neighbouring steps "
                         "overlap)") if world == 1 else
                        ("fp64_emu.dist.ShardedHostStream (disjoint host shares, NVLink all-gathers, overlapped "

@@ -46,6 +46,29 @@ def gpu_local_cpus(device=None):
         return None
 
 
+class gpu_local_allocation:
+    """Context manager: while active, this process runs on the cores local to
+    `device`, so page-locked buffers allocated inside it are placed on the
+    GPU's NUMA node; the previous CPU affinity is restored on exit (copies
+    keep using the buffers' placement, whichever cores later run).
+    .cpus: the cores used, or None when NVML could not tell."""
+
+    def __init__(self, device=None):
+        self.device = device
+        self.cpus = None
+        self._old = None
+
+    def __enter__(self):
+        self._old = os.sched_getaffinity(0)
+        self.cpus = bind_to_gpu_cpus(self.device)
+        return self
+
+    def __exit__(self, *exc):
+        if self._old is not None:
+            os.sched_setaffinity(0, self._old)
+        return False
+
+
 def bind_to_gpu_cpus(device=None):
     """Restrict this process to the cores local to `device`, so page-locked
     buffers allocated afterwards are first touched on the GPU's NUMA node and

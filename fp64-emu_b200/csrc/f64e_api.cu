@@ -793,9 +793,12 @@ int run_pipelined(const Plan& l, const ModTables& T, const View& f, void* ws, co
   const int e_aux = ne++;
   cudaEventRecord(E[e_aux], pr->aux);
   int rc = F64E_OK;
+  // F64E_PIPE_GEMM_STREAMS=1: every GEMM chunk on one stream, so no two GEMM
+  // launches are ever resident at once (A/B checks).
+  const bool one_gemm_stream = env_int("F64E_PIPE_GEMM_STREAMS") == 1;
   const int e_gemm = ne;
   for (int u = 0; u < U; u++) {
-    cudaStream_t h = pr->hi[u & 1];
+    cudaStream_t h = pr->hi[one_gemm_stream ? 0 : (u & 1)];
     if (need[u] >= 0) cudaStreamWaitEvent(h, E[need[u]], 0);
     if (2 * u + 1 < ngev) cudaEventRecord(static_cast<cudaEvent_t>(gev[2 * u]), h);
     if (rc == F64E_OK) rc = launch_gemm_view(l, T, units[u], tA[u], tB[u], ws, d, h);

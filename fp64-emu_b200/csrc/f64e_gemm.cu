@@ -333,14 +333,19 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     tma_prefetch_desc(&tmapB);
   }
   __syncwarp();
-  if (warp == 1) {
-    tmem_alloc_pair(tmem_slot, TMEM_COLS);
-    tmem_relinquish_pair();
-  }
+  // TMEM of the pair: both CTAs' warp 1 allocate collectively, and only once
+  // both CTAs are running (the first cluster barrier); the permit is given up
+  // after the second, when both allocations have completed.  Measured on
+  // B200: allocating before the peer CTA was known to be live, or giving up
+  // the pair's permit right after one's own allocation, occasionally left the
+  // peer's allocation blocked for good (a stalled product, no wait run out).
+  cluster_sync();
+  if (warp == 1) tmem_alloc_pair(tmem_slot, TMEM_COLS);
   tc_fence_before();
   __syncwarp();
   cluster_sync();
   tc_fence_after();
+  if (warp == 1) tmem_relinquish_pair();
   const uint32_t tmem_base = *tmem_slot;
   const uint64_t lim = g.wait_limit_ns;
   const uint32_t full0 = mapa_shared(smem_u32(&full_bar[0]), 0);     // leader's full barriers

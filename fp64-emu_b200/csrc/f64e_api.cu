@@ -753,28 +753,14 @@ int run_pipelined(const Plan& l, const ModTables& T, const View& f, void* ws, co
   std::vector<int> need(U, -1);
   std::lock_guard<std::mutex> lk(pr->mtx);
   cudaEvent_t* E = pr->ev;
-  int ne = 3;   // E[0] = fork, E[1] / E[2] = head fork / join
+  int ne = 1;   // E[0] = fork
   // Head, on the caller's stream: everything the first GEMM unit reads (and
   // the first H row chunks of A).
   const int H = (ch.by_batch || J > 1) ? 1 : std::max(1, std::min(C, ch.head));
-  // F64E_PIPE_HEAD2=1 extracts the head's A chunks on a second stream beside
-  // B's extraction (A/B checks).
-  const bool head2 = env_int("F64E_PIPE_HEAD2") == 1;
-  cudaError_t e = cudaSuccess;
-  if (head2) {
-    e = cudaEventRecord(E[1], s);
-    if (e == cudaSuccess) e = cudaStreamWaitEvent(pr->aux, E[1], 0);
-    if (e != cudaSuccess) return cuda_fail(e, "pipeline head fork");
-  }
-  for (int c = 0; c < H; c++) extract_A(l, T, rows[c], ws, 0, l.K, head2 ? pr->aux : s);
+  for (int c = 0; c < H; c++) extract_A(l, T, rows[c], ws, 0, l.K, s);
   if (ch.by_batch) extract_B(l, T, rows[0], ws, 0, l.K, s);
   else extract_B(l, T, J > 1 ? bcols[0] : f, ws, 0, l.K, s);
-  if (head2) {
-    e = cudaEventRecord(E[2], pr->aux);
-    if (e == cudaSuccess) e = cudaStreamWaitEvent(s, E[2], 0);
-    if (e != cudaSuccess) return cuda_fail(e, "pipeline head join");
-  }
-  e = cudaEventRecord(E[0], s);
+  cudaError_t e = cudaEventRecord(E[0], s);
   for (int i = 0; i < 2 && e == cudaSuccess; i++) e = cudaStreamWaitEvent(pr->hi[i], E[0], 0);
   if (e == cudaSuccess) e = cudaStreamWaitEvent(pr->aux, E[0], 0);
   if (e != cudaSuccess) return cuda_fail(e, "pipeline fork");

@@ -65,9 +65,10 @@ WORKLOADS = {
     "C5": ("bmm_nt", 64, 1024, 1024, 1024, "unif", None, None),
     # profiling case: same kernels as C2 at a quarter of the device footprint
     "P4096": ("mm_nt", 1, 4096, 4096, 4096, "randn", None, None),
-    # one rank's block of C2 / C4 on eight GPUs (2 x 4 grid), alone on one GPU:
-    # the per-rank timeline of the scaling runs
+    # one rank's block of C2 / C4 on eight GPUs (2 x 4 grid; C2blk8t: the 4 x 2
+    # grid's block), alone on one GPU: the per-rank timeline of the scaling runs
     "C2blk8": ("mm_nt", 1, 4096, 2048, 8192, "randn", None, None),
+    "C2blk8t": ("mm_nt", 1, 2048, 4096, 8192, "randn", None, None),
     "C4blk8": ("mm_nt", 1, 8192, 4096, 16384, "wide30", None, None),
 }
 
@@ -330,6 +331,16 @@ def barrier():
         dist.barrier()
 
 
+def gather_ranks(obj):
+    """Every rank's `obj`, in rank order (one all_gather_object, outside
+    timing)."""
+    if not dist.is_initialized():
+        return [obj]
+    out = [None] * dist.get_world_size()
+    dist.all_gather_object(out, obj)
+    return out
+
+
 def max_over_ranks(x):
     if not dist.is_initialized():
         return x
@@ -468,6 +479,15 @@ def run_ours(args):
     ends = [ev[i + 1][0] for i in range(args.steps - 1)] + [t_stop]
     tl = [Step.timeline(ev[i], launches[i], ev[i][0].elapsed_time(ends[i])) for i in range(args.steps)]
     head_local, gaps_local, tail_local = (sum(x[k] for x in tl) / args.steps for k in range(3))
+    # this rank's last timed step: its GEMM launches as (start, end) in ms from
+    # the step's start, on the rank's own clock
+    last = ev[-1]
+    chunks_last = [(round(last[0].elapsed_time(last[1 + 2 * i]), 4), round(last[0].elapsed_time(last[2 + 2 * i]), 4))
+                   for i in range(launches[-1])]
+    per_rank = gather_ranks({"rank": rank, "ms_per_step": round(ms_local, 4), "gemm_busy": round(gemm_ms_local, 4),
+                             "head": round(head_local, 4), "gaps": round(gaps_local, 4),
+                             "tail": round(tail_local, 4), "last_step_gemm_ms": chunks_last,
+                             "block": [int(A_l.shape[-2]), int(B_l.shape[-1] if nt else B_l.shape[-2])]})
 
     # e2e through the public API with host buffers.
     import fp64_emu
@@ -594,6 +614,10 @@ def run_ours(args):
     }
     if world > 1:
         result["operand_broadcast_s"] = round(bcast_s, 3)
+        if args.timeline_out and rank == 0:
+            with open(args.timeline_out, "w") as f:
+                json.dump({"workload": args.workload, "n_gpus": world, "steps": args.steps,
+                           "ms_per_step_max": round(ms, 4), "clocks": clk, "per_rank": per_rank}, f, indent=1)
     if rank == 0 and world == 1 and not args.no_cpu and batch == 1 and nt:
         try:
             result["cpu_baseline"] = cpu_baseline_oracle(A_host_full, B_host_full, nprimes, corr,
@@ -923,6 +947,62 @@ def run_pcie_probe(args):
               flush=True)
 
 
+def run_recon_l2_probe(args):
+    """How much an L2-resident reconstruction could save (the bound on fusing
+    the reconstruction into the GEMM, or ordering the GEMM's work so that a
+    panel's residue planes are read back before they leave L2).  For row
+    blocks of C2's shape (rows x 8192, K = 8192, default plan): sizing,
+    extraction and the GEMM once, then the reconstruction phase alone,
+    (a) right after the GEMM wrote the planes ("after_gemm"), (b) after a
+    write of a buffer twice the L2's size ("cold"), (c) straight after another
+    reconstruction of the same block ("hot": planes and output in L2).  CUDA
+    events around the reconstruction launch only; every output is checked equal
+    bit for bit."""
+    from fp64_emu.dist import PHASE_EXTRACT, PHASE_GEMM, PHASE_RECON, PHASE_SIZING, ShardedProduct
+    dev = torch.device("cuda", torch.cuda.current_device())
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    res = []
+    for rows in (256, 512, 2048):
+        A, B = make_inputs("randn", 1, rows, 8192, 8192, True, dev, seed=args.seed)
+        sp = ShardedProduct(A, B, True, 8192, 8192)
+        out = torch.empty(rows, 8192, dtype=torch.float64, device=dev)
+        sp._phase(out, PHASE_SIZING)
+        sp._phase(out, PHASE_EXTRACT | PHASE_GEMM)   # unchunked: every phase sees the whole block
+        sp._phase(out, PHASE_RECON)
+        ref = out.clone()
+        import fp64_emu
+        same = torch.equal(fp64_emu.mm_nt(A, B).view(torch.int64), ref.view(torch.int64))
+        t = {"after_gemm": [], "cold": [], "hot": []}
+
+        def timed(key):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            sp._phase(out, PHASE_RECON)
+            e1.record()
+            torch.cuda.synchronize()
+            t[key].append(e0.elapsed_time(e1) * 1e3)
+
+        for i in range(args.steps):
+            sp._phase(out, PHASE_GEMM)
+            timed("after_gemm")
+            flush.fill_(i & 255)
+            timed("cold")
+            timed("hot")
+            same = same and torch.equal(out.view(torch.int64), ref.view(torch.int64))
+        G = sp.primes.numel() + (2 if sp.corr else 0)
+        plane_bytes = rows * 8192 * (sp.primes.numel() + 4)   # residue bytes + one int32 correction
+        med = {k: statistics.median(v) for k, v in t.items()}
+        res.append({"rows": rows, "elements": rows * 8192, "plane_bytes": plane_bytes,
+                    "out_bytes": rows * 8192 * 8, "int8_gemms": G,
+                    "us": {k: round(v, 2) for k, v in med.items()},
+                    "gbs": {k: round((plane_bytes + rows * 8192 * 8) / (v * 1e-6) / 1e9, 1) for k, v in med.items()},
+                    "bit_identical": same})
+        del sp, out, ref, A, B
+        torch.cuda.empty_cache()
+    print(json.dumps({"recon_l2_probe": res, "steps": args.steps,
+                      "note": "median reconstruction launch time; L2 126 MB"}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -943,6 +1023,11 @@ def main():
     ap.add_argument("--pcie-probe", action="store_true",
                     help="measure every rank's pinned host <-> device copy rates at once and exit")
     ap.add_argument("--probe-mib", type=int, default=1024)
+    ap.add_argument("--recon-l2-probe", action="store_true",
+                    help="time the reconstruction of C2-shaped row blocks with its planes in L2 and not, and exit")
+    ap.add_argument("--timeline-out", default=None,
+                    help="N>1: rank 0 writes every rank's per-step phases and its last step's GEMM launch times "
+                         "(JSON) to this path")
     ap.add_argument("--peak-n", type=int, default=8192)
     ap.add_argument("--peak-seconds", type=float, default=4.0)
     args = ap.parse_args()
@@ -959,6 +1044,8 @@ def main():
             run_int8_peak(args)
         elif args.pcie_probe:
             run_pcie_probe(args)
+        elif args.recon_l2_probe:
+            run_recon_l2_probe(args)
         elif args.impl == "reference":
             run_reference(args)
         else:

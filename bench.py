@@ -70,7 +70,14 @@ WORKLOADS = {
     "C2blk8": ("mm_nt", 1, 4096, 2048, 8192, "randn", None, None),
     "C2blk8t": ("mm_nt", 1, 2048, 4096, 8192, "randn", None, None),
     "C4blk8": ("mm_nt", 1, 8192, 4096, 16384, "wide30", None, None),
+    # deep K: four 65536-deep segments (15 moduli + correction), the reference's
+    # segmented path on its side
+    "D1": ("mm", 1, 2048, 2048, 262144, "randn", None, None),
 }
+
+# Above this depth the double-double accuracy sample (one launch per K step)
+# would take minutes; both arms skip it there and say so.
+ACCURACY_MAX_K = 65536
 
 
 def log(*a):
@@ -630,7 +637,9 @@ def run_ours(args):
             result["cpu_fp64_torch"] = {"value": None, "error": str(e)[:200]}
     if rank == 0 and not args.no_native:
         result["native_dgemm"] = native_dgemm(A_l, B_l, nt, args)
-    if rank == 0 and not args.no_accuracy:
+    if rank == 0 and not args.no_accuracy and K > ACCURACY_MAX_K:
+        result["accuracy"] = {"skipped": f"K = {K} > {ACCURACY_MAX_K}: one double-double launch per K step"}
+    elif rank == 0 and not args.no_accuracy:
         try:
             result["accuracy"] = accuracy_sample(kind, A_l, B_l, step.out, args.workload, world,
                                                  others={"native_dgemm": lambda a, b: a @ b})
@@ -819,7 +828,9 @@ def run_reference(args):
                           "value": sample_sha256(C0, args.workload, world)},
         "clocks": clk,
     }
-    if not args.no_accuracy:
+    if not args.no_accuracy and K > ACCURACY_MAX_K:
+        result["accuracy"] = {"skipped": f"K = {K} > {ACCURACY_MAX_K}: one double-double launch per K step"}
+    elif not args.no_accuracy:
         try:
             result["accuracy"] = accuracy_sample(kind, A, B, C0, args.workload, world)
         except Exception as e:  # noqa: BLE001

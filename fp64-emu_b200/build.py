@@ -3,6 +3,12 @@
   fp64_emu/libf64e.so          CUDA kernels + C ABI (include/f64e.h), sm_100a
   fp64_emu/_fp64_emu_b200.so   torch op binding (namespace fp64_emu_b200),
                                linked against libf64e.so
+  fp64_emu/libf64e_debug.so    the same C ABI built with F64E_DEBUG_BOUNDS:
+                               every extraction, GEMM-epilogue and
+                               reconstruction access checked against its
+                               buffer, misses recorded in the status word and
+                               skipped (a checking build for callers of the C
+                               ABI; nothing loads it by default)
 
 Both land inside the package directory, so they travel with the working tree
 and are found without any install step.  Usage: python fp64-emu_b200/build.py
@@ -33,6 +39,7 @@ NVCC_FLAGS = ["-std=c++17", "-O3", "-lineinfo", "-gencode", "arch=compute_100a,c
               "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden", "-ccbin", CXX,
               f"-I{INCLUDE}", f"-I{CSRC}"]
 LIB = PKG / "libf64e.so"
+LIB_DEBUG = PKG / "libf64e_debug.so"
 EXT = PKG / "_fp64_emu_b200.so"
 
 
@@ -53,21 +60,24 @@ def _run(cmd, verbose):
     return r
 
 
-def build_lib(force=False, verbose=False, extra_nvcc=()):
-    OBJ.mkdir(exist_ok=True)
+def build_lib(force=False, verbose=False, extra_nvcc=(), debug=False):
+    obj_dir = OBJ / "debug" if debug else OBJ
+    lib = LIB_DEBUG if debug else LIB
+    flags = NVCC_FLAGS + (["-DF64E_DEBUG_BOUNDS"] if debug else []) + list(extra_nvcc)
+    obj_dir.mkdir(parents=True, exist_ok=True)
     hdrs = [CSRC / h for h in HEADERS] + [INCLUDE / "f64e.h"]
     jobs = []
     for src in CUDA_SOURCES:
-        o = OBJ / (Path(src).stem + ".o")
+        o = obj_dir / (Path(src).stem + ".o")
         if force or not _newer(o, [CSRC / src] + hdrs):
-            jobs.append([NVCC, "-c", CSRC / src, "-o", o] + NVCC_FLAGS + list(extra_nvcc))
+            jobs.append([NVCC, "-c", CSRC / src, "-o", o] + flags)
     with cf.ThreadPoolExecutor(max_workers=min(8, os.cpu_count() or 1)) as ex:
         list(ex.map(lambda c: _run(c, verbose), jobs))
-    objs = [OBJ / (Path(s).stem + ".o") for s in CUDA_SOURCES]
-    if force or jobs or not _newer(LIB, objs):
-        _run([NVCC, "-shared", "-o", LIB] + objs + ["-gencode", "arch=compute_100a,code=sm_100a",
+    objs = [obj_dir / (Path(s).stem + ".o") for s in CUDA_SOURCES]
+    if force or jobs or not _newer(lib, objs):
+        _run([NVCC, "-shared", "-o", lib] + objs + ["-gencode", "arch=compute_100a,code=sm_100a",
                                                      "-cudart", "shared", "-ccbin", CXX], verbose)
-    return LIB
+    return lib
 
 
 def build_ext(force=False, verbose=False):
@@ -91,6 +101,7 @@ def build_ext(force=False, verbose=False):
 def build(force=False, verbose=False):
     build_lib(force, verbose)
     build_ext(force, verbose)
+    build_lib(force, verbose, debug=True)
 
 
 if __name__ == "__main__":
@@ -103,4 +114,4 @@ if __name__ == "__main__":
         build_lib(a.force, a.v)
     else:
         build(a.force, a.v)
-    print("built", LIB, "" if a.lib_only else EXT)
+    print("built", LIB, "" if a.lib_only else f"{EXT} {LIB_DEBUG}")

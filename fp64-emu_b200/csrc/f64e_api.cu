@@ -440,6 +440,16 @@ View batch_chunk(const Plan& l, const View& f, int64_t b0, int64_t b1) {
   return v;
 }
 
+int64_t env_int(const char* name);
+
+// [base + off, base + off + bytes) as a Span (debug bounds build).
+Span span_of(const void* base, size_t off, size_t bytes) {
+  Span sp;
+  sp.lo = reinterpret_cast<uintptr_t>(base) + off;
+  sp.hi = sp.lo + bytes;
+  return sp;
+}
+
 ExtractArgs extract_args(const Plan& l, void* ws, int64_t k0, int64_t kw) {
   ExtractArgs ea{};
   ea.K = kw;
@@ -449,6 +459,7 @@ ExtractArgs extract_args(const Plan& l, void* ws, int64_t k0, int64_t kw) {
   ea.maxlg = at<WsHead>(ws, 0)->maxlg;
   ea.bits = l.bits;
   ea.use_corr = l.use_corr;
+  ea.status = &at<WsHead>(ws, 0)->status;
   return ea;
 }
 
@@ -464,6 +475,8 @@ ExtractArgs extract_A_args(const Plan& l, const View& v, void* ws, int64_t k0, i
   ea.q_plane = l.P + 1;
   ea.planes = v.pA;
   ea.pstride = ea.rows * l.Kp;
+  ea.src = span_of(v.A, 0, sizeof(double) * (size_t)ea.rows * (size_t)ea.ld);
+  ea.dst = span_of(ws, l.o_pA, (size_t)l.G * l.MF * l.Kp);
   return ea;
 }
 
@@ -484,6 +497,10 @@ ExtractArgs extract_B_args(const Plan& l, const View& v, void* ws, int64_t k0, i
   eb.hi_plane = l.P + 1;
   eb.planes = v.pB;
   eb.pstride = v.batch * v.b_zrows * l.Kp;
+  // [K][N] layout: member b's element (k, n) at X[(b K + k) ld + n]; [N][K]: rows of pitch ld
+  const size_t nel = l.nt ? (size_t)((v.batch * eb.K - 1) * eb.ld + v.N) : (size_t)eb.rows * (size_t)eb.ld;
+  eb.src = span_of(v.B, 0, (v.batch > 0 && v.N > 0 && eb.K > 0) ? sizeof(double) * nel : 0);
+  eb.dst = span_of(ws, l.o_pB, (size_t)l.G * l.NF * l.Kp);
   return eb;
 }
 
@@ -520,6 +537,8 @@ GemmArgs gemm_args(const Plan& l, const View& v, void* ws) {
   g.corr = v.corr;
   g.status = &at<WsHead>(ws, 0)->status;
   g.wait_limit_ns = g_wait_limit.load();
+  g.res_span = span_of(ws, l.o_res, (size_t)l.P * l.MF * l.ldn);
+  g.corr_span = span_of(ws, l.o_corr, sizeof(int32_t) * ncorr_planes(l) * l.MF * l.ldn);
   return g;
 }
 
@@ -575,6 +594,19 @@ void run_reconstruct(const Plan& l, const ModTables& T, const View& v, void* ws,
   r.exact = l.exact;
   r.C = v.C;
   r.ldc = v.ldc;
+  r.status = &at<WsHead>(ws, 0)->status;
+  r.res_span = span_of(ws, l.o_res, (size_t)l.P * l.MF * l.ldn);
+  r.corr_span = corr_mode == 3 ? span_of(ws, l.o_cacc, sizeof(int64_t) * l.MF * l.ldn)
+                               : span_of(ws, l.o_corr, sizeof(int32_t) * ncorr_planes(l) * l.MF * l.ldn);
+  r.out_span = span_of(v.C, 0, r.MF > 0 ? sizeof(double) * (size_t)((r.MF - 1) * v.ldc + v.N) : 0);
+#ifdef F64E_DEBUG_BOUNDS
+  // Self-test hook of the checking build: F64E_DEBUG_SHRINK_OUT_BYTES=n moves
+  // the end of the output range n bytes in, so the writes of the last
+  // elements are reported (site 20) and skipped.  Those elements lie inside
+  // the caller's output, so no access leaves the real buffers either way.
+  const int64_t shrink = env_int("F64E_DEBUG_SHRINK_OUT_BYTES");
+  if (shrink > 0) r.out_span.hi -= std::min<uintptr_t>((uintptr_t)shrink, r.out_span.hi - r.out_span.lo);
+#endif
   launch_reconstruct(r, T, s, beside_gemm, sms);
 }
 

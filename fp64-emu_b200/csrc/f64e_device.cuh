@@ -22,6 +22,13 @@ enum : int {
   kWaitAccEmpty = 4,  // MMA issuer waiting for the epilogue to drain TMEM
   kWaitDrain = 5,     // teardown waiting for in-flight copies / MMAs
   kWaitSelfTest = 9,  // f64e_wait_selftest: a barrier nothing arrives at
+  // Bounds sites, recorded only by a library built with F64E_DEBUG_BOUNDS:
+  // the access lay outside the range its launcher gave, and was skipped.
+  kBoundsExtractLoad = 16,   // extraction: operand read
+  kBoundsExtractStore = 17,  // extraction: plane write
+  kBoundsGemmStore = 18,     // GEMM epilogue: residue or correction write
+  kBoundsReconLoad = 19,     // reconstruction: residue or correction read
+  kBoundsReconStore = 20,    // reconstruction: output write
 };
 
 __device__ __forceinline__ uint64_t globaltimer_ns() {
@@ -32,6 +39,22 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
 
 __device__ __forceinline__ void record_status(int* status, int code) {
   if (status) atomicCAS(status, 0, code);
+}
+
+// Debug bounds check: true when [p, p + bytes) lies inside s.  A library built
+// with F64E_DEBUG_BOUNDS records `site` in the status word on a miss (first
+// writer wins) and the caller skips the access; no trap, so the context stays
+// usable.  In the release build the check compiles away.
+__device__ __forceinline__ bool in_span(const void* p, size_t bytes, const Span& s, int* status, int site) {
+#ifdef F64E_DEBUG_BOUNDS
+  const uintptr_t a = reinterpret_cast<uintptr_t>(p);
+  if (a >= s.lo && a + bytes <= s.hi && a + bytes >= a) return true;
+  record_status(status, site);
+  return false;
+#else
+  (void)p; (void)bytes; (void)s; (void)status; (void)site;
+  return true;
+#endif
 }
 
 // ----------------------------------------------------------------- sizing --

@@ -209,6 +209,12 @@ __device__ __forceinline__ void extract8(const double (&x)[8], int s, bool fast,
   constexpr int PMAX = NP > 0 ? NP : kMaxP;
   const int P = NP > 0 ? NP : T.P;
   const int64_t pstride = a.pstride;
+  // Debug bounds build: the group's first and last plane bound every store
+  // (planes ascend with their index); on a miss no plane is written.
+  if (!in_span(dst, 8, a.dst, a.status, kBoundsExtractStore) ||
+      !in_span(dst + (int64_t)max(P - 1, corr ? max(a.hi_plane, a.q_plane) : 0) * pstride, 8, a.dst, a.status,
+               kBoundsExtractStore))
+    return;
   Split S[8];
   const uint64_t bias = 1ULL << be;
   uint32_t top = 0;
@@ -257,6 +263,9 @@ __device__ __forceinline__ void extract_rows_body(const ExtractArgs& a, const Mo
     const double* __restrict__ xr = a.X + r * a.ld + a.koff;
     for (int64_t ch = (int64_t)bx * 32 + tx; ch < nch; ch += (int64_t)gdx * 32) {
       const int64_t k0 = ch << 3;
+      if (k0 < a.K && !in_span(xr + k0, 8 * (size_t)(a.K - k0 < 8 ? a.K - k0 : 8), a.src, a.status,
+                               kBoundsExtractLoad))
+        continue;
       double x[8];
       if (VEC && k0 + 8 <= a.K) {
         const double2* p2 = reinterpret_cast<const double2*>(xr + k0);
@@ -313,7 +322,8 @@ __device__ __forceinline__ void extract_cols_body(const ExtractArgs& a, const Mo
 #pragma unroll
     for (int i = 0; i < 8; i++) {
       const int64_t k = k0 + w + 8 * i;
-      v[i] = (nin && k < a.K) ? __ldg(xb + k * a.ld) : 0.0;
+      v[i] = (nin && k < a.K && in_span(xb + k * a.ld, 8, a.src, a.status, kBoundsExtractLoad)) ? __ldg(xb + k * a.ld)
+                                                                                                 : 0.0;
     }
 #pragma unroll
     for (int i = 0; i < 8; i++) xs[lane * kColPitch + w + 8 * i] = v[i];

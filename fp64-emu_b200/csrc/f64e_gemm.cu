@@ -243,9 +243,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             w[i] = x;
           }
           const int col = tl.n0 + c * 32;
-          if (row_ok && col < g.ldn)
+          if (row_ok && col < g.ldn && in_span(orow + col, 16, g.res_span, g.status, kBoundsGemmStore))
             *reinterpret_cast<uint4*>(orow + col) = make_uint4(w[0], w[1], w[2], w[3]);
-          if (row_ok && col + 16 < g.ldn)
+          if (row_ok && col + 16 < g.ldn &&
+              in_span(orow + col + 16, 16, g.res_span, g.status, kBoundsGemmStore))
             *reinterpret_cast<uint4*>(orow + col + 16) = make_uint4(w[4], w[5], w[6], w[7]);
         }
       } else {
@@ -258,7 +259,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           const int col = tl.n0 + c * 32;
 #pragma unroll
           for (int i = 0; i < 8; i++)
-            if (row_ok && col + 4 * i < g.ldn)
+            if (row_ok && col + 4 * i < g.ldn &&
+                in_span(orow + col + 4 * i, 16, g.corr_span, g.status, kBoundsGemmStore))
               *reinterpret_cast<uint4*>(orow + col + 4 * i) = make_uint4(v[4 * i], v[4 * i + 1], v[4 * i + 2],
                                                                          v[4 * i + 3]);
         }
@@ -451,9 +453,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             w[i] = x;
           }
           const int col = tl.n0 + c * 32;
-          if (row_ok && col < g.ldn)
+          if (row_ok && col < g.ldn && in_span(orow + col, 16, g.res_span, g.status, kBoundsGemmStore))
             *reinterpret_cast<uint4*>(orow + col) = make_uint4(w[0], w[1], w[2], w[3]);
-          if (row_ok && col + 16 < g.ldn)
+          if (row_ok && col + 16 < g.ldn &&
+              in_span(orow + col + 16, 16, g.res_span, g.status, kBoundsGemmStore))
             *reinterpret_cast<uint4*>(orow + col + 16) = make_uint4(w[4], w[5], w[6], w[7]);
         }
       } else {
@@ -466,7 +469,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           const int col = tl.n0 + c * 32;
 #pragma unroll
           for (int i = 0; i < 8; i++)
-            if (row_ok && col + 4 * i < g.ldn)
+            if (row_ok && col + 4 * i < g.ldn &&
+                in_span(orow + col + 4 * i, 16, g.corr_span, g.status, kBoundsGemmStore))
               *reinterpret_cast<uint4*>(orow + col + 4 * i) = make_uint4(v[4 * i], v[4 * i + 1], v[4 * i + 2],
                                                                          v[4 * i + 3]);
         }

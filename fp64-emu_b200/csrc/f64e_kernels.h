@@ -46,6 +46,8 @@ struct ExtractArgs {
   int hi_plane, q_plane;  // plane indices of the correction digits
   int8_t* planes;
   int64_t pstride;      // bytes from one plane to the next
+  Span src, dst;        // the operand's elements, the planes' bytes (debug bounds build)
+  int* status;          // status word (debug bounds build)
 };
 struct ExtractPair {
   ExtractArgs a[2];
@@ -68,6 +70,7 @@ struct GemmArgs {
   int32_t* corr;       // [1 or 2][batch][M][ldn]
   int* status;
   uint64_t wait_limit_ns;
+  Span res_span, corr_span;   // output ranges (debug bounds build)
 };
 // 3-D map (Kp, rows, zdim) of K-major int8 planes; consecutive z-slices are
 // zrows * Kp bytes apart (zrows = rows when 0).
@@ -102,6 +105,8 @@ struct ReconArgs {
   int bits, exact;
   double* C;             // [batch * M][N], row pitch ldc
   int64_t ldc;
+  Span res_span, corr_span, out_span;   // debug bounds build
+  int* status;                          // debug bounds build
 };
 // beside_gemm: the launch runs beside a resident GEMM chunk (picks the form
 // that takes less from it).

@@ -57,6 +57,13 @@ struct ModTables {
   uint64_t crtL[2];            // L as a 128-bit two's complement (lo, hi)
 };
 
+// Byte range [lo, hi) a kernel may touch through one pointer.  Filled by the
+// launchers in every build; only a library built with F64E_DEBUG_BOUNDS checks
+// accesses against it (in_span, f64e_device.cuh).
+struct Span {
+  uintptr_t lo = 0, hi = 0;
+};
+
 // Device-resident scalars at the head of every workspace.  maxlg holds the
 // operand maxima of the per-row / per-column log2 norms; in a partitioned
 // multi-GPU run they are MAX-all-reduced between the sizing and compute

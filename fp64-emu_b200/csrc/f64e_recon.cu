@@ -153,6 +153,32 @@ __device__ __forceinline__ void load_corr(const ReconArgs& a, int64_t off, int64
   }
 }
 
+// Debug bounds build: the reads and the write of one four-column group (the
+// first and the last residue plane bound the planes between them).  False,
+// with the site recorded, when any lies outside its launcher's range; the
+// caller then skips the group.  Always true in the release build.
+template <int CM>
+__device__ __forceinline__ bool recon_group_in_span(const ReconArgs& a, int64_t off, int64_t plane, int P,
+                                                    int64_t i, int64_t j0) {
+#ifdef F64E_DEBUG_BOUNDS
+  bool ok = in_span(a.res + off, 4, a.res_span, a.status, kBoundsReconLoad) &&
+            in_span(a.res + (int64_t)(P - 1) * plane + off, 4, a.res_span, a.status, kBoundsReconLoad);
+  if (CM == 1) ok = ok && in_span(static_cast<const int32_t*>(a.corr) + off, 16, a.corr_span, a.status,
+                                  kBoundsReconLoad);
+  if (CM == 2) ok = ok && in_span(static_cast<const int32_t*>(a.corr) + off, 16, a.corr_span, a.status,
+                                  kBoundsReconLoad) &&
+                    in_span(static_cast<const int32_t*>(a.corr) + plane + off, 16, a.corr_span, a.status,
+                            kBoundsReconLoad);
+  if (CM == 3) ok = ok && in_span(static_cast<const int64_t*>(a.corr) + off, 32, a.corr_span, a.status,
+                                  kBoundsReconLoad);
+  const int64_t nc = a.N - j0 < 4 ? a.N - j0 : 4;
+  return ok && in_span(a.C + i * a.ldc + j0, 8 * (size_t)nc, a.out_span, a.status, kBoundsReconStore);
+#else
+  (void)a; (void)off; (void)plane; (void)P; (void)i; (void)j0;
+  return true;
+#endif
+}
+
 }  // namespace
 
 // General form (any moduli): balanced digits, reduction with one correction.
@@ -172,6 +198,7 @@ __global__ void __launch_bounds__(256) reconstruct_kernel(const ReconArgs a, con
     for (int64_t jq = (int64_t)blockIdx.x * 64 + threadIdx.x; jq < nq; jq += (int64_t)gridDim.x * 64) {
       const int64_t j0 = jq << 2;
       const int64_t off = i * a.ldn + j0;
+      if (!recon_group_in_span<CM>(a, off, plane, P, i, j0)) continue;
       int32_t dp[4][kGroups];
 #pragma unroll
       for (int e = 0; e < 4; e++)
@@ -263,6 +290,7 @@ __global__ void __launch_bounds__(256, 2) reconstruct_fast_kernel(const ReconArg
     for (int64_t jq = (int64_t)blockIdx.x * 64 + threadIdx.x; jq < nq; jq += (int64_t)gridDim.x * 64) {
       const int64_t j0 = jq << 2;
       const int64_t off = i * a.ldn + j0;
+      if (!recon_group_in_span<CM>(a, off, plane, P, i, j0)) continue;
       uint32_t rw[PMAX];
 #pragma unroll
       for (int t = 0; t < PMAX; t++)
@@ -385,6 +413,7 @@ __global__ void __launch_bounds__(256, 4) reconstruct_crt_kernel(const ReconArgs
     for (int64_t jq = (int64_t)blockIdx.x * 64 + threadIdx.x; jq < nq; jq += (int64_t)gridDim.x * 64) {
       const int64_t j0 = jq << 2;
       const int64_t off = i * a.ldn + j0;
+      if (!recon_group_in_span<CM>(a, off, plane, P, i, j0)) continue;
       uint32_t rw[kMaxP];
 #pragma unroll
       for (int t = 0; t < kMaxP; t++)
@@ -472,6 +501,7 @@ __global__ void __launch_bounds__(256, MINB) reconstruct_f64_kernel(const ReconA
     for (int64_t jq = (int64_t)blockIdx.x * 64 + threadIdx.x; jq < nq; jq += (int64_t)gridDim.x * 64) {
       const int64_t j0 = jq << 2;
       const int64_t off = i * a.ldn + j0;
+      if (!recon_group_in_span<CM>(a, off, plane, P, i, j0)) continue;
       const int8_t* rp = a.res + off;
       uint32_t rw[PMAX];
 #pragma unroll

@@ -153,7 +153,13 @@ F64E_API int f64e_mm_timed(double* out, float* times, const double* A, const dou
 
 /* Device status word of a workspace: 0, or the site code of the first bounded
  * wait that ran out in the last product run with it.  Synchronizes the
- * stream.  Returns F64E_OK / F64E_ERR_*. */
+ * stream.  Returns F64E_OK / F64E_ERR_*.
+ * In the checking build (libf64e_debug.so, compiled with F64E_DEBUG_BOUNDS;
+ * same ABI) the word also takes the first out-of-range access, which the
+ * kernel skipped instead of performing: 16 extraction read, 17 extraction
+ * write, 18 GEMM epilogue write, 19 reconstruction read, 20 reconstruction
+ * write.  The reference has no such build; it stands in for the device-side
+ * bounds checks a sanitizer would give. */
 F64E_API int f64e_status(const void* workspace, void* stream, int32_t* status);
 
 /* Limit, in nanoseconds, on every device-side wait of the GEMM (default

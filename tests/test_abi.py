@@ -66,6 +66,28 @@ def test_library_exports_every_declared_symbol(lib):
         assert hasattr(lib, n), n
 
 
+def test_checking_build_exports_the_same_abi():
+    # libf64e_debug.so (F64E_DEBUG_BOUNDS) is a drop-in for libf64e.so
+    dbg = os.path.join(ROOT, "fp64-emu_b200", "fp64_emu", "libf64e_debug.so")
+    if not os.path.exists(dbg):
+        import subprocess
+        import sys
+        subprocess.run([sys.executable, "-c",
+                        "import sys; sys.path.insert(0, %r); import build; build.build_lib(debug=True)"
+                        % os.path.join(ROOT, "fp64-emu_b200")], check=True)
+    L = ctypes.CDLL(dbg)
+    for n in declared_symbols():
+        assert hasattr(L, n), n
+    L.f64e_workspace_size.argtypes = [ctypes.POINTER(Problem)]
+    L.f64e_workspace_size.restype = ctypes.c_size_t
+    arr = (ctypes.c_int32 * 14)(*PRIMES[:14])
+    p = Problem(1, 300, 200, 100, 0, 14, arr, 1, 53, 1, 0)
+    want = ctypes.CDLL(LIB)
+    want.f64e_workspace_size.argtypes = [ctypes.POINTER(Problem)]
+    want.f64e_workspace_size.restype = ctypes.c_size_t
+    assert L.f64e_workspace_size(ctypes.byref(p)) == want.f64e_workspace_size(ctypes.byref(p)) > 0
+
+
 def test_maxp(lib):
     assert lib.f64e_maxp() == 20
 

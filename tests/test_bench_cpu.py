@@ -1,6 +1,7 @@
 """bench.py's host-side pieces on the CPU: the workload table, seeded inputs,
 the peak and traffic figures it reads from committed files, and the launch
 count it claims per step."""
+import json
 import os
 import sys
 
@@ -94,3 +95,35 @@ def test_sample_digest_is_of_the_sample_bytes():
     assert bench.sample_sha256(C2, "C2", 1) == hashlib.sha256(C2[:256].contiguous().numpy().tobytes()).hexdigest()
     C5 = torch.randn(3, 300, 40, dtype=torch.float64)   # batches: member 0's first 256 rows
     assert bench.sample_sha256(C5, "C5", 8) == hashlib.sha256(C5[0, :256].contiguous().numpy().tobytes()).hexdigest()
+
+
+def _gather_worker(rank, world, port, outdir):
+    import torch.distributed as dist
+    from datetime import timedelta
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    if ROOT not in sys.path:
+        sys.path.insert(0, ROOT)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=60))
+    try:
+        import bench
+        got = bench.gather_ranks({"rank": rank, "ms_per_step": 1.0 + rank, "last_step_gemm_ms": [(0.1 * rank, 0.2)]})
+        with open(os.path.join(outdir, f"r{rank}.json"), "w") as f:
+            json.dump(got, f)
+    finally:
+        dist.destroy_process_group()
+
+
+def test_per_rank_timeline_gather_on_gloo_ranks(tmp_path):
+    # the per-rank timeline (--timeline-out) gathers every rank's record in rank order
+    import socket
+    import torch.multiprocessing as mp
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    mp.start_processes(_gather_worker, args=(2, port, str(tmp_path)), nprocs=2, join=True, start_method="spawn")
+    for r in range(2):
+        got = json.load(open(tmp_path / f"r{r}.json"))
+        assert [g["rank"] for g in got] == [0, 1]
+        assert [g["ms_per_step"] for g in got] == [1.0, 2.0]

@@ -448,12 +448,13 @@ def run_ours(args):
     A_host_full = A.cpu() if (rank == 0 and world == 1 and not args.no_cpu) else None
     B_host_full = B.cpu() if (rank == 0 and world == 1 and not args.no_cpu) else None
     shs = shares = host_cpus = None
-    if world > 1 and batch == 1:
-        # e2e at N > 1: every rank copies in a disjoint share of its blocks and
-        # the blocks are completed over NVLink (fp64_emu.dist.ShardedHostStream)
+    if world > 1:
+        # e2e at N > 1 (fp64_emu.dist.ShardedHostStream): every rank copies in
+        # a disjoint share of its blocks and the blocks are completed over
+        # NVLink; batches: every rank copies in its own members
         from fp64_emu.dist import ShardedHostStream
         from fp64_emu.host import gpu_local_allocation
-        shs = ShardedHostStream(kind, M, N, K, nprimes=nprimes, corr=corr)
+        shs = ShardedHostStream(kind, M, N, K, nprimes=nprimes, corr=corr, batch=batch)
         with gpu_local_allocation(dev) as loc:   # page-locked shares on the GPU's NUMA node
             shares = shs.host_shares(A.cpu(), B.cpu())
             host_cpus = loc.cpus
@@ -505,26 +506,16 @@ def run_ours(args):
             B_pin = B_l.cpu().pin_memory()
             out_pin = torch.empty(step.out.shape, dtype=torch.float64).pin_memory()
             host_cpus = loc.cpus
-        A_d = torch.empty_like(A_l)
-        B_d = torch.empty_like(B_l)
 
     hs = fp64_emu.HostStream(kind, nprimes=nprimes, corr=corr) if world == 1 else None
 
     def e2e_step():
         if shs is not None:
             shs.submit(*shares)
-            return
-        if hs is not None:
+        else:
             # a stream of host-resident products: the operand copies, the
             # product and the result copy of neighbouring steps overlap
             hs.submit(A_pin, B_pin, out_pin)
-            return
-        A_d.copy_(A_pin, non_blocking=True)
-        B_d.copy_(B_pin, non_blocking=True)
-        from fp64_emu.dist import ShardedProduct
-        C = torch.empty(step.out.shape, dtype=torch.float64, device=dev)
-        ShardedProduct(A_d, B_d, nt, slab_cols, K, nprimes=nprimes, corr=corr).run(C)
-        out_pin.copy_(C, non_blocking=True)
 
     e2e_steps = max(3, min(args.steps, 20))
     for _ in range(2):
@@ -553,7 +544,7 @@ def run_ours(args):
     e2e_ms = max_over_ranks(e2e_ms_local)
     # whole job, summed over ranks: the shares copied in, the blocks copied out
     if shs is not None:
-        h2d, d2h = (M * K + K * N) * 8, M * N * 8
+        h2d, d2h = batch * (M * K + K * N) * 8, batch * M * N * 8
     else:
         h2d, d2h = (A_l.numel() + B_l.numel()) * 8 * world, step.out.numel() * 8 * world
 
@@ -596,8 +587,9 @@ def run_ours(args):
                                  if host_cpus else "page-locked, default placement"),
                 "api": ("fp64_emu.HostStream (operand copies, product and result copy of neighbouring steps "
                         "overlap)") if world == 1 else
-                       ("fp64_emu.dist.ShardedHostStream (disjoint host shares, NVLink all-gathers, overlapped "
-                        "stages)" if shs is not None else "fp64_emu.dist.ShardedProduct with explicit copies")},
+                       ("fp64_emu.dist.ShardedHostStream (disjoint host shares, "
+                        + ("each rank's own batch members" if batch > 1 else "NVLink all-gathers")
+                        + ", overlapped stages)")},
         "gpu_launches": sum(our_kernel_launches_per_step(kind, A_l.shape[0] if A_l.dim() == 3 else 1, c, Ml, Nl, Kl)
                             for c in launches),
         "roofline": {"bound": "tensor", "kernel": "residue_gemm_pair_kernel" if Ml > 128 else "residue_gemm_tc_kernel",

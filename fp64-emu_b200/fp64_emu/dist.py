@@ -149,17 +149,35 @@ class ShardedHostStream:
     With `depth` buffer sets in rotation on four streams (copy in, gather,
     compute, copy out), neighbouring products overlap stage by stage.
 
+    Batched products ("bmm_nt", "bmm"; batch > 1) are split by batch member
+    instead: each rank copies in its own members' operands, so nothing needs
+    gathering, and the stages are copy in, sizing with the MAX all-reduce and
+    product, copy out.
+
     Host layout: `host_shares(A, B)` cuts a full host A and B into this rank's
     shares (once, outside any timed loop); submit(a_share, b_share, c_block)
     takes page-locked CPU tensors shaped like those shares and this rank's C
-    block.  kind: "mm_nt" (B given as [K, N]) or "mm" (B as [N, K])."""
+    block.  kind: "mm_nt" (B given as [K, N]) or "mm" (B as [N, K]), or their
+    batched forms "bmm_nt" ([batch, K, N]) and "bmm" ([batch, N, K])."""
 
-    def __init__(self, kind, M, N, K, nprimes=None, exact=True, bits=53, corr=None, depth=2):
-        if kind not in ("mm", "mm_nt"):
-            raise ValueError("kind must be mm or mm_nt")
-        self.kind, self.b_kn = kind, kind == "mm_nt"
-        self.M, self.N, self.K = M, N, K
+    def __init__(self, kind, M, N, K, nprimes=None, exact=True, bits=53, corr=None, depth=2, batch=1):
+        if kind not in ("mm", "mm_nt", "bmm", "bmm_nt"):
+            raise ValueError("kind must be mm, mm_nt, bmm or bmm_nt")
+        self.batched = kind in ("bmm", "bmm_nt")
+        if self.batched != (batch > 1):
+            raise ValueError("bmm / bmm_nt take batch > 1, mm / mm_nt batch = 1")
+        self.kind, self.b_kn = kind, kind in ("mm_nt", "bmm_nt")
+        self.M, self.N, self.K, self.batch = M, N, K, batch
         self.world, self.rank = dist.get_world_size(), dist.get_rank()
+        if self.batched:
+            self.m0, self.m1 = block_range(batch, self.world, self.rank)
+            self.nprimes, self.exact, self.bits, self.corr = nprimes, exact, bits, corr
+            self.depth = max(1, int(depth))
+            self.dev = torch.device("cuda", torch.cuda.current_device())
+            self.streams = [torch.cuda.Stream(self.dev) for _ in range(4)]
+            self.slots = [None] * self.depth
+            self.n = 0
+            return
         self.pr, self.pc = grid_shape(self.world)
         self.gi, self.gj = divmod(self.rank, self.pc)
         (self.r0, self.r1), (self.c0, self.c1) = rank_block(self.rank, self.world, M, N)
@@ -192,7 +210,14 @@ class ShardedHostStream:
 
     def host_shares(self, A, B):
         """This rank's page-locked shares of full host operands A [M, K] and
-        B ([K, N] or [N, K]), and a page-locked C block to receive results."""
+        B ([K, N] or [N, K]), and a page-locked C block to receive results
+        (batched: this rank's members of A, B and C)."""
+        if self.batched:
+            m0, m1 = self.m0, self.m1
+            a = A[m0:m1].contiguous().pin_memory()
+            b = B[m0:m1].contiguous().pin_memory()
+            c = torch.empty(m1 - m0, self.M, self.N, dtype=torch.float64).pin_memory()
+            return a, b, c
         a0, a1 = self.a_share_range()
         b0, b1 = self.b_share_range()
         blk = B[:, self.c0:self.c1] if self.b_kn else B[self.c0:self.c1]
@@ -205,6 +230,8 @@ class ShardedHostStream:
         s = self.slots[k]
         if s is not None:
             return s
+        if self.batched:
+            return self._batch_slot(k)
         dev, K = self.dev, self.K
         bshape_full = (K, self.nb) if self.b_kn else (self.nb, K)
         with torch.cuda.stream(self.streams[2]):
@@ -223,10 +250,55 @@ class ShardedHostStream:
         self.slots[k] = s
         return s
 
+    def _batch_slot(self, k):
+        dev, K, M, N = self.dev, self.K, self.M, self.N
+        nb = self.m1 - self.m0
+        with torch.cuda.stream(self.streams[2]):
+            s = {"A": torch.empty(nb, M, K, dtype=torch.float64, device=dev),
+                 "B": torch.empty((nb, K, N) if self.b_kn else (nb, N, K), dtype=torch.float64, device=dev),
+                 "C": torch.empty(nb, M, N, dtype=torch.float64, device=dev)}
+            # the column-slab rule runs over all members' columns, as on one GPU
+            s["sp"] = ShardedProduct(s["A"], s["B"], self.b_kn, self.batch * N, K, nprimes=self.nprimes,
+                                     exact=self.exact, bits=self.bits, corr=self.corr)
+        for name in ("loaded", "computed", "done"):
+            s[name] = torch.cuda.Event()
+        s["used"] = False
+        self.slots[k] = s
+        return s
+
+    def _submit_batched(self, a_share, b_share, c_block):
+        h2d, _, comp, d2h = self.streams
+        s = self._slot(self.n % self.depth)
+        cur = torch.cuda.current_stream(self.dev)
+        for st in self.streams:
+            st.wait_stream(cur)
+        if s["used"]:
+            h2d.wait_event(s["computed"])   # the operands were read by the product
+            comp.wait_event(s["done"])      # the C members left the device
+        with torch.cuda.stream(h2d):
+            s["A"].copy_(a_share, non_blocking=True)
+            s["B"].copy_(b_share, non_blocking=True)
+            s["loaded"].record(h2d)
+        comp.wait_event(s["loaded"])
+        with torch.cuda.stream(comp):
+            sp = s["sp"]
+            sp.sizing(s["C"])    # MAX all-reduce of the operand maxima over all ranks
+            sp._phase(s["C"], PHASE_COMPUTE)
+            s["computed"].record(comp)
+        d2h.wait_event(s["computed"])
+        with torch.cuda.stream(d2h):
+            c_block.copy_(s["C"], non_blocking=True)
+            s["done"].record(d2h)
+        s["used"] = True
+        self.n += 1
+        return c_block
+
     def submit(self, a_share, b_share, c_block):
         """Queue this rank's part of one product; every rank calls submit in
         the same order.  Returns at once; c_block holds the rank's C block
         after synchronize()."""
+        if self.batched:
+            return self._submit_batched(a_share, b_share, c_block)
         h2d, comm, comp, d2h = self.streams
         s = self._slot(self.n % self.depth)
         cur = torch.cuda.current_stream(self.dev)

@@ -102,14 +102,13 @@ def _host_worker(rank, world, port, case, outdir):
                             device_id=torch.device("cuda", rank))
     try:
         from fp64_emu.dist import ShardedHostStream
-        kind, M, K, N = case
+        kind, M, K, N = case[:4]
+        batch = case[4] if len(case) > 4 else 1
         g = torch.Generator().manual_seed(321)
         outs = []
-        hs = ShardedHostStream(kind, M, N, K, depth=2)
+        hs = ShardedHostStream(kind, M, N, K, depth=2, batch=batch)
         for step in range(3):   # three products through the rotating buffers
-            A = torch.randn(M, K, dtype=torch.float64, generator=g)
-            B = torch.randn((K, N) if kind == "mm_nt" else (N, K), dtype=torch.float64, generator=g) * 2.0 ** step
-            A[M // 2:] = 1.0
+            A, B = _host_operands(kind, M, K, N, batch, step, g)
             a, b, c = hs.host_shares(A, B)
             hs.submit(a, b, c)
             outs.append(c)
@@ -120,7 +119,26 @@ def _host_worker(rank, world, port, case, outdir):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("case", [("mm_nt", 700, 1500, 900), ("mm", 520, 640, 333)])
+def _host_operands(kind, M, K, N, batch, step, g):
+    """Host operands of one product of the stream test: A's second half of rows
+    (of every member) flattened to 1.0, so the ranks' operand maxima differ
+    and the MAX all-reduce decides the width."""
+    b_kn = kind in ("mm_nt", "bmm_nt")
+    shpA = (batch, M, K) if batch > 1 else (M, K)
+    shpB = (K, N) if b_kn else (N, K)
+    if batch > 1:
+        shpB = (batch,) + shpB
+    A = torch.randn(shpA, dtype=torch.float64, generator=g)
+    B = torch.randn(shpB, dtype=torch.float64, generator=g) * 2.0 ** step
+    if batch > 1:
+        A[batch // 2:] = 1.0
+    else:
+        A[M // 2:] = 1.0
+    return A, B
+
+
+@pytest.mark.parametrize("case", [("mm_nt", 700, 1500, 900), ("mm", 520, 640, 333), ("bmm_nt", 200, 300, 150, 6),
+                                  ("bmm", 130, 260, 70, 5)])
 def test_sharded_host_stream_matches_single_gpu(case, tmp_path):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
@@ -130,14 +148,16 @@ def test_sharded_host_stream_matches_single_gpu(case, tmp_path):
                        start_method="spawn")
     import fp64_emu
     from fp64_emu.dist import rank_block
-    kind, M, K, N = case
+    kind, M, K, N = case[:4]
+    batch = case[4] if len(case) > 4 else 1
     g = torch.Generator().manual_seed(321)
     blocks = [torch.load(tmp_path / f"hblock{r}.pt") for r in range(world)]
     for step in range(3):
-        A = torch.randn(M, K, dtype=torch.float64, generator=g)
-        B = torch.randn((K, N) if kind == "mm_nt" else (N, K), dtype=torch.float64, generator=g) * 2.0 ** step
-        A[M // 2:] = 1.0
+        A, B = _host_operands(kind, M, K, N, batch, step, g)
         full = getattr(fp64_emu, kind)(A.cuda(), B.cuda()).cpu()
+        if batch > 1:
+            assert torch.equal(torch.cat([blocks[r][step] for r in range(world)]), full)
+            continue
         for r in range(world):
             (r0, r1), (c0, c1) = rank_block(r, world, M, N)
             assert torch.equal(blocks[r][step], full[r0:r1, c0:c1])
